@@ -1,0 +1,49 @@
+// Internal helpers shared by the runtime shim and the operator launch files.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+
+#include "hc_ops.h"
+#include "hc_runtime.h"
+
+namespace hc {
+
+// Records `status` with a printf-style message as the calling thread's last error and
+// returns the status, so call sites can `return fail(HC_ERR_INVALID, "...")`.
+int fail(int status, const char* fmt, ...);
+
+// Clears the thread's last error and returns HC_OK.
+int ok();
+
+// Converts a CUDA error into HC_ERR_CUDA with the call site in the message.
+int cuda_fail(cudaError_t err, const char* what);
+
+// Host-side fault injection (HC_FAULT="<call>:<n>").  Returns true when this call of
+// `kind` ("malloc", "memcpy", "launch") must fail.
+bool fault_hit(const char* kind);
+
+// SM count of the current device (cached per device).
+int sm_count();
+
+// Size in bytes of one element of an hc_dtype, 0 for an unknown value.
+size_t dtype_size(int dtype);
+
+// Checks a kernel launch: returns HC_OK or HC_ERR_CUDA naming `kernel`.
+int check_launch(const char* kernel);
+
+// Device error words: files whose kernels contain bounded spin-waits register a reader that
+// copies and clears their word.  A non-zero word is reported by hc_check_device_error().
+typedef uint32_t (*error_word_reader)(const char** kernel_name);
+void register_error_word(error_word_reader reader);
+
+}  // namespace hc
+
+#define HC_CHECK_CUDA(call)                                          \
+    do {                                                             \
+        cudaError_t hc_err__ = (call);                               \
+        if (hc_err__ != cudaSuccess) return hc::cuda_fail(hc_err__, #call); \
+    } while (0)

@@ -1,0 +1,160 @@
+// Host-buffer runners: copy inputs in, launch, copy outputs out, with the transfers of one
+// chunk overlapping the kernel of the previous one.
+//
+// Mirrors the reference's host-pointer runner contract
+// (ops/flash_attention_fwd_fused/runner/flash_attention_fwd_fused_runner.hpp:9-18 and the
+// device branch of ops/elementwise_add/runner/elementwise_add_runner.cpp:16-38, which copies
+// in, launches and copies out), with the difference that the device staging memory is a
+// caller-owned workspace instead of per-call allocations.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "hc_internal.h"
+
+namespace hc {
+namespace {
+
+// Three internal streams per device (copy-in, compute, copy-out) and the events that chain them;
+// created once per device and kept for the life of the process.
+struct Pipe {
+    bool ready = false;
+    cudaStream_t in = nullptr, comp = nullptr, out = nullptr;
+    cudaEvent_t in_done[2] = {nullptr, nullptr}, comp_done[2] = {nullptr, nullptr}, out_done[2] = {nullptr, nullptr};
+    cudaEvent_t start = nullptr;
+};
+
+std::mutex g_pipe_mu;
+Pipe g_pipes[64];
+
+int get_pipe(Pipe** out) {
+    int dev = 0;
+    HC_CHECK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(HC_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_pipe_mu);
+    Pipe& p = g_pipes[dev];
+    if (!p.ready) {
+        HC_CHECK_CUDA(cudaStreamCreateWithFlags(&p.in, cudaStreamNonBlocking));
+        HC_CHECK_CUDA(cudaStreamCreateWithFlags(&p.comp, cudaStreamNonBlocking));
+        HC_CHECK_CUDA(cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking));
+        for (int b = 0; b < 2; ++b) {
+            HC_CHECK_CUDA(cudaEventCreateWithFlags(&p.in_done[b], cudaEventDisableTiming));
+            HC_CHECK_CUDA(cudaEventCreateWithFlags(&p.comp_done[b], cudaEventDisableTiming));
+            HC_CHECK_CUDA(cudaEventCreateWithFlags(&p.out_done[b], cudaEventDisableTiming));
+        }
+        HC_CHECK_CUDA(cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming));
+        p.ready = true;
+    }
+    *out = &p;
+    return HC_OK;
+}
+
+struct FaChunking {
+    uint64_t bh, heads_per_chunk, q_head_bytes, kv_head_bytes, o_head_bytes, lse_head_bytes, slot_bytes;
+};
+
+int fa_chunking(const flash_attention_fwd_fused_tiling_data* t, int dtype, FaChunking* c) {
+    size_t es = dtype_size(dtype);
+    if (es == 0 || dtype == HC_DTYPE_I32 || dtype == HC_DTYPE_I8 || dtype == HC_DTYPE_U8)
+        return fail(HC_ERR_UNSUPPORTED, "flash_attention host runner: dtype %d", dtype);
+    c->bh = static_cast<uint64_t>(t->B) * t->H;
+    c->q_head_bytes = static_cast<uint64_t>(t->S_q) * t->D * es;
+    c->kv_head_bytes = static_cast<uint64_t>(t->S_k) * t->D * es + static_cast<uint64_t>(t->S_k) * t->D_v * es;
+    c->o_head_bytes = static_cast<uint64_t>(t->S_q) * t->D_v * es;
+    c->lse_head_bytes = static_cast<uint64_t>(t->S_q) * sizeof(float);
+    uint64_t per_head = c->q_head_bytes + c->kv_head_bytes;
+    // ~96 MB of inputs per chunk: big enough to keep the copy engines streaming, small enough
+    // that the first and last chunks (which cannot overlap) are a few percent of the job.
+    uint64_t h = (96ull << 20) / (per_head ? per_head : 1);
+    if (h < 1) h = 1;
+    if (h > c->bh) h = c->bh;
+    c->heads_per_chunk = h;
+    auto align = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
+    c->slot_bytes = align(h * c->q_head_bytes) + align(h * static_cast<uint64_t>(t->S_k) * t->D * es) +
+                    align(h * static_cast<uint64_t>(t->S_k) * t->D_v * es) + align(h * c->o_head_bytes) +
+                    align(h * c->lse_head_bytes);
+    return HC_OK;
+}
+
+}  // namespace
+}  // namespace hc
+
+using namespace hc;
+
+extern "C" int hc_flash_attention_fwd_fused_host_workspace_size(const flash_attention_fwd_fused_tiling_data* t,
+                                                                int dtype, size_t* bytes) {
+    if (!t || !bytes) return fail(HC_ERR_INVALID, "flash_attention host workspace: null argument");
+    FaChunking c;
+    int rc = fa_chunking(t, dtype, &c);
+    if (rc) return rc;
+    *bytes = static_cast<size_t>(2 * c.slot_bytes);
+    return ok();
+}
+
+extern "C" int hc_flash_attention_fwd_fused_host(const void* h_q, const void* h_k, const void* h_v, void* h_o,
+                                                 float* h_lse, const flash_attention_fwd_fused_tiling_data* t,
+                                                 int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+    if (!t) return fail(HC_ERR_INVALID, "flash_attention host: null tiling");
+    if (!h_q || !h_k || !h_v || !h_o || !workspace) return fail(HC_ERR_INVALID, "flash_attention host: null pointer");
+    FaChunking c;
+    int rc = fa_chunking(t, dtype, &c);
+    if (rc) return rc;
+    if (workspace_bytes < 2 * c.slot_bytes)
+        return fail(HC_ERR_INVALID, "flash_attention host: workspace %zu B < required %llu B", workspace_bytes,
+                    static_cast<unsigned long long>(2 * c.slot_bytes));
+    if (c.bh == 0 || t->S_q == 0) return ok();
+    Pipe* pp = nullptr;
+    rc = get_pipe(&pp);
+    if (rc) return rc;
+    Pipe& P = *pp;
+    const size_t es = dtype_size(dtype);
+    auto align = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
+    const uint64_t h = c.heads_per_chunk;
+    const uint64_t k_bytes_h = static_cast<uint64_t>(t->S_k) * t->D * es;
+    const uint64_t v_bytes_h = static_cast<uint64_t>(t->S_k) * t->D_v * es;
+    uint8_t* slot[2];
+    slot[0] = static_cast<uint8_t*>(workspace);
+    slot[1] = slot[0] + c.slot_bytes;
+    cudaStream_t user = static_cast<cudaStream_t>(stream);
+    HC_CHECK_CUDA(cudaEventRecord(P.start, user));
+    HC_CHECK_CUDA(cudaStreamWaitEvent(P.in, P.start, 0));
+    const uint64_t nchunks = (c.bh + h - 1) / h;
+    for (uint64_t ci = 0; ci < nchunks; ++ci) {
+        const int b = static_cast<int>(ci & 1);
+        const uint64_t h0 = ci * h;
+        const uint64_t hn = (h0 + h <= c.bh) ? h : (c.bh - h0);
+        uint8_t* dq = slot[b];
+        uint8_t* dk = dq + align(h * c.q_head_bytes);
+        uint8_t* dv = dk + align(h * k_bytes_h);
+        uint8_t* dO = dv + align(h * v_bytes_h);
+        float* dl = reinterpret_cast<float*>(dO + align(h * c.o_head_bytes));
+        // Copy-in of this chunk may start once the copy-out of the chunk that used this slot
+        // two steps ago is finished (which also implies its kernel finished).
+        if (ci >= 2) HC_CHECK_CUDA(cudaStreamWaitEvent(P.in, P.out_done[b], 0));
+        if (fault_hit("memcpy")) return fail(HC_ERR_INJECTED, "flash_attention host: injected copy failure");
+        HC_CHECK_CUDA(cudaMemcpyAsync(dq, static_cast<const uint8_t*>(h_q) + h0 * c.q_head_bytes, hn * c.q_head_bytes,
+                                      cudaMemcpyHostToDevice, P.in));
+        HC_CHECK_CUDA(cudaMemcpyAsync(dk, static_cast<const uint8_t*>(h_k) + h0 * k_bytes_h, hn * k_bytes_h,
+                                      cudaMemcpyHostToDevice, P.in));
+        HC_CHECK_CUDA(cudaMemcpyAsync(dv, static_cast<const uint8_t*>(h_v) + h0 * v_bytes_h, hn * v_bytes_h,
+                                      cudaMemcpyHostToDevice, P.in));
+        HC_CHECK_CUDA(cudaEventRecord(P.in_done[b], P.in));
+        HC_CHECK_CUDA(cudaStreamWaitEvent(P.comp, P.in_done[b], 0));
+        flash_attention_fwd_fused_tiling_data tc = *t;
+        tc.B = 1;
+        tc.H = static_cast<uint32_t>(hn);
+        rc = hc_flash_attention_fwd_fused_launch(dq, dk, dv, dO, h_lse ? dl : nullptr, &tc, dtype, P.comp);
+        if (rc) return rc;
+        HC_CHECK_CUDA(cudaEventRecord(P.comp_done[b], P.comp));
+        HC_CHECK_CUDA(cudaStreamWaitEvent(P.out, P.comp_done[b], 0));
+        HC_CHECK_CUDA(cudaMemcpyAsync(static_cast<uint8_t*>(h_o) + h0 * c.o_head_bytes, dO, hn * c.o_head_bytes,
+                                      cudaMemcpyDeviceToHost, P.out));
+        if (h_lse)
+            HC_CHECK_CUDA(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(h_lse) + h0 * c.lse_head_bytes, dl,
+                                          hn * c.lse_head_bytes, cudaMemcpyDeviceToHost, P.out));
+        HC_CHECK_CUDA(cudaEventRecord(P.out_done[b], P.out));
+    }
+    HC_CHECK_CUDA(cudaStreamWaitEvent(user, P.out_done[(nchunks - 1) & 1], 0));
+    HC_CHECK_CUDA(cudaStreamSynchronize(P.out));
+    return hc_check_device_error();
+}

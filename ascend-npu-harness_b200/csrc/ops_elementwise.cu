@@ -1,0 +1,256 @@
+// Elementwise ladder operators: elementwise_add, axpy_scalar_affine, broadcast_binary,
+// activation_gelu_silu.  All are HBM-bound streams: 16-byte packs, grid-stride loops sized to
+// the SM count, no tensor cores.
+//
+// Arithmetic follows the reference goldens operation by operation, with explicitly rounded
+// fp32 intrinsics so the compiler cannot contract a*b+c into one FMA (the goldens are compiled
+// for x86-64 without FMA, so each product and sum is rounded separately):
+//   elementwise_add      ops/elementwise_add/golden/elementwise_add_golden.cpp:12-14
+//   axpy_scalar_affine   ops/axpy_scalar_affine/golden/axpy_scalar_affine_golden.cpp:13-15
+//   broadcast_binary     ops/broadcast_binary/golden/broadcast_binary_golden.cpp:28-40
+//   activation_gelu_silu ops/activation_gelu_silu/golden/activation_gelu_silu_golden.cpp:16-49
+#include <cuda_runtime.h>
+
+#include "hc_device.cuh"
+#include "hc_internal.h"
+
+namespace hc {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+int grid_for(size_t work_items) {
+    size_t blocks = (work_items + kThreads * kUnroll - 1) / (kThreads * kUnroll);
+    size_t cap = static_cast<size_t>(sm_count()) * 8;  // 8 x 256 threads = 2048 resident per SM
+    if (blocks > cap) blocks = cap;
+    if (blocks == 0) blocks = 1;
+    return static_cast<int>(blocks);
+}
+
+// ---------------------------------------------------------------------------------------
+// Generic unary/binary maps.  Op::apply(float a, float b) -> float.
+// ---------------------------------------------------------------------------------------
+template <typename T, typename Op>
+__global__ void __launch_bounds__(kThreads) map2_vec_kernel(const T* __restrict__ a, const T* __restrict__ b,
+                                                            T* __restrict__ out, size_t n, Op op) {
+    constexpr int P = elem<T>::kPack;
+    const size_t packs = n / P;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const pack<T>* pa = reinterpret_cast<const pack<T>*>(a);
+    const pack<T>* pb = reinterpret_cast<const pack<T>*>(b);
+    pack<T>* po = reinterpret_cast<pack<T>*>(out);
+    size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; i + (kUnroll - 1) * stride < packs; i += kUnroll * stride) {
+        pack<T> va[kUnroll], vb[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            va[u] = ld_stream(pa + i + u * stride);
+            if (Op::kBinary) vb[u] = ld_stream(pb + i + u * stride);
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            pack<T> r;
+#pragma unroll
+            for (int e = 0; e < P; ++e)
+                r.v[e] = elem<T>::from_f(op.apply(elem<T>::to_f(va[u].v[e]), Op::kBinary ? elem<T>::to_f(vb[u].v[e]) : 0.f));
+            st_stream(po + i + u * stride, r);
+        }
+    }
+    for (; i < packs; i += stride) {
+        pack<T> va = ld_stream(pa + i);
+        pack<T> vb;
+        if (Op::kBinary) vb = ld_stream(pb + i);
+        pack<T> r;
+#pragma unroll
+        for (int e = 0; e < P; ++e)
+            r.v[e] = elem<T>::from_f(op.apply(elem<T>::to_f(va.v[e]), Op::kBinary ? elem<T>::to_f(vb.v[e]) : 0.f));
+        st_stream(po + i, r);
+    }
+    // Tail elements that do not fill a pack.
+    const size_t tail0 = packs * P;
+    const size_t gtid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (gtid < n - tail0) {
+        size_t j = tail0 + gtid;
+        out[j] = elem<T>::from_f(op.apply(elem<T>::to_f(a[j]), Op::kBinary ? elem<T>::to_f(b[j]) : 0.f));
+    }
+}
+
+// Scalar variant for buffers that are not 16-byte aligned.
+template <typename T, typename Op>
+__global__ void __launch_bounds__(kThreads) map2_scalar_kernel(const T* __restrict__ a, const T* __restrict__ b,
+                                                               T* __restrict__ out, size_t n, Op op) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t j = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += stride)
+        out[j] = elem<T>::from_f(op.apply(elem<T>::to_f(a[j]), Op::kBinary ? elem<T>::to_f(b[j]) : 0.f));
+}
+
+struct AddOp {
+    static constexpr bool kBinary = true;
+    // One fp32 add, then one rounding to the storage type.  For fp16/bf16 inputs the fp32 sum
+    // is exact-or-correctly-rounded with p=24 >= 2p'+2, so the result equals the correctly
+    // rounded 16-bit addition (what __hadd2 computes).
+    __device__ float apply(float x, float y) const { return __fadd_rn(x, y); }
+};
+
+struct AxpyOp {
+    static constexpr bool kBinary = false;
+    float alpha, beta;
+    __device__ float apply(float x, float) const { return __fadd_rn(__fmul_rn(alpha, x), beta); }
+};
+
+struct ActOp {
+    static constexpr bool kBinary = false;
+    uint32_t act;  // 0 = GELU (tanh form), 1 = SiLU
+    __device__ float apply(float v, float) const {
+        if (act == 0) {
+            const float kSqrt2OverPi = 0.7978845608f;
+            const float kGeluCoeff = 0.044715f;
+            float x3 = __fmul_rn(__fmul_rn(v, v), v);
+            float inner = __fmul_rn(kSqrt2OverPi, __fadd_rn(v, __fmul_rn(kGeluCoeff, x3)));
+            float t = tanhf(inner);
+            return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, t));
+        }
+        if (v >= 0.0f) {
+            float e = expf(-v);
+            return __fdiv_rn(v, __fadd_rn(1.0f, e));
+        }
+        float e = expf(v);
+        return __fdiv_rn(__fmul_rn(v, e), __fadd_rn(1.0f, e));
+    }
+};
+
+template <typename T, typename Op>
+int launch_map(const void* a, const void* b, void* out, size_t n, Op op, void* stream, const char* name) {
+    if (n == 0) return ok();
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const T* ta = static_cast<const T*>(a);
+    const T* tb = static_cast<const T*>(b);
+    T* to = static_cast<T*>(out);
+    bool vec = aligned16(a) && aligned16(out) && (!Op::kBinary || aligned16(b));
+    if (vec) {
+        size_t packs = n / elem<T>::kPack;
+        map2_vec_kernel<T, Op><<<grid_for(packs > 0 ? packs : 1), kThreads, 0, s>>>(ta, tb, to, n, op);
+    } else {
+        map2_scalar_kernel<T, Op><<<grid_for(n), kThreads, 0, s>>>(ta, tb, to, n, op);
+    }
+    return check_launch(name);
+}
+
+template <typename Op>
+int dispatch_map(int dtype, const void* a, const void* b, void* out, size_t n, Op op, void* stream, const char* name) {
+    switch (dtype) {
+        case HC_DTYPE_F32: return launch_map<float, Op>(a, b, out, n, op, stream, name);
+        case HC_DTYPE_F16: return launch_map<f16_t, Op>(a, b, out, n, op, stream, name);
+        case HC_DTYPE_BF16: return launch_map<bf16_t, Op>(a, b, out, n, op, stream, name);
+        default: return fail(HC_ERR_UNSUPPORTED, "%s: dtype %d not supported (F32, F16, BF16)", name, dtype);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// broadcast_binary: z = x * y[yb, c] + bias[c]
+// ---------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(kThreads) broadcast_vec_kernel(const T* __restrict__ x, const T* __restrict__ y,
+                                                                 const T* __restrict__ bias, T* __restrict__ z,
+                                                                 uint32_t C, size_t hw, size_t chw, bool y_per_batch,
+                                                                 size_t n) {
+    constexpr int P = elem<T>::kPack;
+    const size_t packs = n / P;
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const pack<T>* px = reinterpret_cast<const pack<T>*>(x);
+    pack<T>* pz = reinterpret_cast<pack<T>*>(z);
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < packs; i += stride) {
+        size_t e0 = i * P;  // hw % P == 0, so the whole pack lies in one (b, c) plane
+        size_t b = e0 / chw;
+        uint32_t c = static_cast<uint32_t>((e0 / hw) % C);
+        float yv = elem<T>::to_f(y[(y_per_batch ? b * C : 0) + c]);
+        float bv = elem<T>::to_f(bias[c]);
+        pack<T> v = ld_stream(px + i);
+        pack<T> r;
+#pragma unroll
+        for (int e = 0; e < P; ++e) r.v[e] = elem<T>::from_f(__fadd_rn(__fmul_rn(elem<T>::to_f(v.v[e]), yv), bv));
+        st_stream(pz + i, r);
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) broadcast_scalar_kernel(const T* __restrict__ x, const T* __restrict__ y,
+                                                                    const T* __restrict__ bias, T* __restrict__ z,
+                                                                    uint32_t C, size_t hw, size_t chw, bool y_per_batch,
+                                                                    size_t n) {
+    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    for (size_t j = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; j < n; j += stride) {
+        size_t b = j / chw;
+        uint32_t c = static_cast<uint32_t>((j / hw) % C);
+        float yv = elem<T>::to_f(y[(y_per_batch ? b * C : 0) + c]);
+        float bv = elem<T>::to_f(bias[c]);
+        z[j] = elem<T>::from_f(__fadd_rn(__fmul_rn(elem<T>::to_f(x[j]), yv), bv));
+    }
+}
+
+template <typename T>
+int launch_broadcast(const void* x, const void* y, const void* bias, void* z, const broadcast_binary_tiling_data* t,
+                     void* stream) {
+    size_t hw = static_cast<size_t>(t->H) * t->W;
+    size_t chw = hw * t->C;
+    size_t n = chw * t->B;
+    bool per_batch = (t->y_batch == t->B) && t->B != 1;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const T* tx = static_cast<const T*>(x);
+    const T* ty = static_cast<const T*>(y);
+    const T* tb = static_cast<const T*>(bias);
+    T* tz = static_cast<T*>(z);
+    if (aligned16(x) && aligned16(z) && hw % elem<T>::kPack == 0) {
+        broadcast_vec_kernel<T><<<grid_for(n / elem<T>::kPack), kThreads, 0, s>>>(tx, ty, tb, tz, t->C, hw, chw, per_batch, n);
+    } else {
+        broadcast_scalar_kernel<T><<<grid_for(n), kThreads, 0, s>>>(tx, ty, tb, tz, t->C, hw, chw, per_batch, n);
+    }
+    return check_launch("broadcast_binary");
+}
+
+}  // namespace
+}  // namespace hc
+
+using namespace hc;
+
+extern "C" int hc_elementwise_add_launch(const void* x, const void* y, void* z, const elementwise_add_tiling_data* t,
+                                         int dtype, void* stream) {
+    if (!t) return fail(HC_ERR_INVALID, "elementwise_add: null tiling");
+    if (t->totalLength && (!x || !y || !z)) return fail(HC_ERR_INVALID, "elementwise_add: null pointer");
+    if (fault_hit("launch")) return fail(HC_ERR_INJECTED, "elementwise_add: injected launch failure");
+    return dispatch_map(dtype, x, y, z, t->totalLength, AddOp{}, stream, "elementwise_add");
+}
+
+extern "C" int hc_axpy_scalar_affine_launch(const void* x, void* y, const axpy_scalar_affine_tiling_data* t, float alpha,
+                                            float beta, int dtype, void* stream) {
+    if (!t) return fail(HC_ERR_INVALID, "axpy_scalar_affine: null tiling");
+    if (t->totalLength && (!x || !y)) return fail(HC_ERR_INVALID, "axpy_scalar_affine: null pointer");
+    if (fault_hit("launch")) return fail(HC_ERR_INJECTED, "axpy_scalar_affine: injected launch failure");
+    return dispatch_map(dtype, x, nullptr, y, t->totalLength, AxpyOp{alpha, beta}, stream, "axpy_scalar_affine");
+}
+
+extern "C" int hc_activation_gelu_silu_launch(const void* x, void* y, const activation_gelu_silu_tiling_data* t,
+                                              int dtype, void* stream) {
+    if (!t) return fail(HC_ERR_INVALID, "activation_gelu_silu: null tiling");
+    if (t->actType > 1) return fail(HC_ERR_INVALID, "activation_gelu_silu: actType %u (0 = GELU, 1 = SiLU)", t->actType);
+    if (t->totalLength && (!x || !y)) return fail(HC_ERR_INVALID, "activation_gelu_silu: null pointer");
+    if (fault_hit("launch")) return fail(HC_ERR_INJECTED, "activation_gelu_silu: injected launch failure");
+    return dispatch_map(dtype, x, nullptr, y, t->totalLength, ActOp{t->actType}, stream, "activation_gelu_silu");
+}
+
+extern "C" int hc_broadcast_binary_launch(const void* x, const void* y, const void* bias, void* z,
+                                          const broadcast_binary_tiling_data* t, int dtype, void* stream) {
+    if (!t) return fail(HC_ERR_INVALID, "broadcast_binary: null tiling");
+    // Same argument checks as ops/broadcast_binary/golden/broadcast_binary_golden.cpp:14-22.
+    if (!x || !y || !bias || !z) return fail(HC_ERR_INVALID, "broadcast_binary: null pointer");
+    if (t->B == 0 || t->C == 0 || t->H == 0 || t->W == 0) return fail(HC_ERR_INVALID, "broadcast_binary: invalid dimensions");
+    if (t->y_batch != 1 && t->y_batch != t->B) return fail(HC_ERR_INVALID, "broadcast_binary: y_batch must be 1 or B");
+    if (fault_hit("launch")) return fail(HC_ERR_INJECTED, "broadcast_binary: injected launch failure");
+    switch (dtype) {
+        case HC_DTYPE_F32: return launch_broadcast<float>(x, y, bias, z, t, stream);
+        case HC_DTYPE_F16: return launch_broadcast<f16_t>(x, y, bias, z, t, stream);
+        case HC_DTYPE_BF16: return launch_broadcast<bf16_t>(x, y, bias, z, t, stream);
+        default: return fail(HC_ERR_UNSUPPORTED, "broadcast_binary: dtype %d not supported", dtype);
+    }
+}
