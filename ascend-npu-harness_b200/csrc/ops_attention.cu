@@ -108,6 +108,77 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x for a pair, on the FMA pipe (offloads the MUFU unit, which would otherwise do as much work
+// per tile as the tensor core).  Range reduction x = n + f with n = rint(x) obtained by adding
+// 1.5*2^23 (the rounded integer lands in the low mantissa bits), f in [-1/2, 1/2]; 2^f by a cubic
+// whose coefficients are the minimax-relative-error fit on [-1/2, 1/2] from the Remez exchange
+// algorithm (max relative error 7.5e-5, below bf16's 2^-9; derivation: csrc/exp2_poly_fit.py);
+// 2^n applied by adding n to the exponent field.  Inputs are clamped to >= -120 so the exponent
+// never underflows; callers only use it where x <= 8.5.
+constexpr float kExp2C0 = 0.99992805719375610f;
+constexpr float kExp2C1 = 0.69326096773147583f;
+constexpr float kExp2C2 = 0.24261112511157990f;
+constexpr float kExp2C3 = 0.05517166852951050f;
+
+// bits(p) + bits(t) * 2^23 as one integer multiply-add (FMA pipe, not the ALU).
+__device__ __forceinline__ float add_exponent(float p, float t) {
+    uint32_t r;
+    asm("mad.lo.u32 %0, %1, 8388608, %2;" : "=r"(r) : "r"(__float_as_uint(t)), "r"(__float_as_uint(p)));
+    return __uint_as_float(r);
+}
+
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+    const float2 kMagic2 = make_float2(12582912.0f, 12582912.0f);  // 1.5 * 2^23
+    const float2 kNegMagic2 = make_float2(-12582912.0f, -12582912.0f);
+    const float2 kMinus1 = make_float2(-1.f, -1.f);
+    x.x = fmaxf(x.x, -120.f);
+    x.y = fmaxf(x.y, -120.f);
+    const float2 t = __fadd2_rn(x, kMagic2);                    // rint(x) in the low mantissa bits
+    const float2 f = __ffma2_rn(__fadd2_rn(t, kNegMagic2), kMinus1, x);  // x - rint(x)
+    float2 p = __ffma2_rn(make_float2(kExp2C3, kExp2C3), f, make_float2(kExp2C2, kExp2C2));
+    p = __ffma2_rn(p, f, make_float2(kExp2C1, kExp2C1));
+    p = __ffma2_rn(p, f, make_float2(kExp2C0, kExp2C0));
+    return make_float2(add_exponent(p.x, t.x), add_exponent(p.y, t.y));
+}
+
+// Register split: the CTA is launched with 168 registers/thread (384 threads x 168 = 64512, the
+// per-SM file allows no more with 12 warps); the two softmax warpgroups then grow to
+// HC_FA_REGS_SOFTMAX (each thread keeps a whole 128-key score row in registers) and the
+// producer/MMA warpgroup shrinks to HC_FA_REGS_CTRL.  ptxas allocates each region with its own
+// budget.
+#ifndef HC_FA_REGS_SOFTMAX
+#define HC_FA_REGS_SOFTMAX 208
+#endif
+#ifndef HC_FA_REGS_CTRL
+#define HC_FA_REGS_CTRL 88
+#endif
+static_assert(2 * 128 * HC_FA_REGS_SOFTMAX + 128 * HC_FA_REGS_CTRL <= 384 * 168,
+              "register split exceeds the registers the CTA is launched with");
+static_assert(HC_FA_REGS_SOFTMAX % 8 == 0 && HC_FA_REGS_CTRL % 8 == 0, "setmaxnreg counts are multiples of 8");
+
+template <int N>
+__device__ __forceinline__ void reg_alloc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void reg_dealloc() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Pairs (c, c+1) of a 128-key row computed with the FMA-pipe exponential: pair index % 8 below
+// HC_FA_POLY_PER8 (the rest go to MUFU ex2).  With MUFU alone the two softmax warpgroups would
+// need as many MUFU cycles per KV tile as the tensor core needs for the four MMAs.
+#ifndef HC_FA_POLY_PER8
+#define HC_FA_POLY_PER8 0
+#endif
+__device__ __forceinline__ constexpr bool poly_pair(int pair) { return (pair & 7) < HC_FA_POLY_PER8; }
+
 template <bool kBF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     if (kBF16) {
@@ -180,12 +251,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sQ = smem_u32(smem + kOffQ);
     const uint32_t sKV = smem_u32(smem + kOffKV);
 
+    if (warp >= 8) {
+        reg_dealloc<HC_FA_REGS_CTRL>();
     if (warp == 9) {
         // ===================================== producer =====================================
         if (lane == 0) {
             uint32_t stage = 0, phase = 0, q_iter = 0;
-            int32_t pending[kStages];
-            for (uint32_t s = 0; s < kStages; ++s) pending[s] = -1;
+            // Copies issued but possibly still in flight: bit s of pend_valid / pend_phase holds
+            // stage s's last load and the barrier phase it completes (bitmasks, not arrays, so
+            // nothing is indexed dynamically in local memory).
+            uint32_t pend_valid = 0, pend_phase = 0;
             int32_t q_pending = -1;
             bool ok = true;
             for (uint32_t u = blockIdx.x; u < p.num_units && ok; u += gridDim.x, ++q_iter) {
@@ -216,7 +291,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tma_load_3d(smem + kOffKV + stage * kTileBytes + h * kHalfBytes, kv ? &tm_v : &tm_k,
                                         &bars->kv_full[stage], static_cast<int32_t>(h * 64),
                                         static_cast<int32_t>(j * kBN), static_cast<int32_t>(bh));
-                        pending[stage] = static_cast<int32_t>(phase);
+                        pend_valid |= 1u << stage;
+                        pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
                         if (++stage == kStages) {
                             stage = 0;
                             phase ^= 1;
@@ -228,8 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // Drain: every TMA copy issued must land before the CTA's shared memory is released.
                 volatile uint32_t never = 0;
                 for (uint32_t s = 0; s < kStages; ++s)
-                    if (pending[s] >= 0)
-                        mbar_wait_bounded(&bars->kv_full[s], static_cast<uint32_t>(pending[s]), &never, &g_fa_error_word,
+                    if (pend_valid & (1u << s))
+                        mbar_wait_bounded(&bars->kv_full[s], (pend_phase >> s) & 1u, &never, &g_fa_error_word,
                                           kErrDrain, 1000000000ull);
                 if (q_pending >= 0)
                     mbar_wait_bounded(&bars->q_full, static_cast<uint32_t>(q_pending), &never, &g_fa_error_word,
@@ -245,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tO[2] = {tmem_base + 256, tmem_base + 384};
             const uint32_t qa[2] = {sQ, sQ + kTileBytes};
             uint32_t stage = 0, phase = 0, q_iter = 0;
-            uint32_t p_par[2] = {0, 0};
+            uint32_t p_par0 = 0, p_par1 = 0;
             bool ok = true;
             auto wait_kv = [&](uint32_t& st) -> bool {
                 if (!mbar_wait_bounded(&bars->kv_full[stage], phase, abort_flag, &g_fa_error_word, kErrMmaKV))
@@ -259,8 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return true;
             };
             auto wait_p = [&](int i) -> bool {
-                if (!mbar_wait_bounded(&bars->p_full[i], p_par[i], abort_flag, &g_fa_error_word, kErrMmaP)) return false;
-                p_par[i] ^= 1;
+                uint32_t& par = i ? p_par1 : p_par0;
+                if (!mbar_wait_bounded(&bars->p_full[i], par, abort_flag, &g_fa_error_word, kErrMmaP)) return false;
+                par ^= 1;
                 tc_fence_after();
                 return true;
             };
@@ -319,7 +396,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             volatile uint32_t never = 0;
             mbar_wait_bounded(&bars->mma_done, 0, &never, &g_fa_error_word, kErrDrain, 1000000000ull);
         }
-    } else if (warp < 8) {
+    }
+    } else {
+        reg_alloc<HC_FA_REGS_SOFTMAX>();
         // ============================== softmax / epilogue ===============================
         const uint32_t wg = warp / 4;                 // Q tile owned by this warpgroup
         const uint32_t r_local = threadIdx.x - wg * 128;  // row within the tile = TMEM lane
@@ -345,13 +424,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 s_par ^= 1;
                 tc_fence_after();
-                uint32_t sr[128];
-                tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(sr + 0));
-                tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
-                tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(sr + 64));
-                tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(sr + 96));
-                tmem_wait_ld();
-                float* s = reinterpret_cast<float*>(sr);
                 const uint32_t kbase = j * kBN;
                 // Valid keys of this tile for this row: causal (k <= row) and sequence tail (k < S_k).
                 int32_t lim = static_cast<int32_t>(p.S_k) - static_cast<int32_t>(kbase);
@@ -359,13 +431,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     int32_t lc = static_cast<int32_t>(row) - static_cast<int32_t>(kbase) + 1;
                     if (lc < lim) lim = lc;
                 }
-                if (lim < static_cast<int32_t>(kBN)) {
+                // Warp-uniform: masked tiles (the causal diagonal, the sequence tail) use MUFU
+                // ex2 for every element so that masked keys give exactly 0.
+                const bool masked = __any_sync(0xffffffffu, lim < static_cast<int32_t>(kBN));
+                // The whole 128-key row of S comes out of TMEM in one round trip (four loads, one
+                // wait) and stays in registers (the warpgroup's setmaxnreg budget allows it).
+                uint32_t sr[128];
 #pragma unroll
-                    for (int c = 0; c < 128; ++c) s[c] = (c < lim) ? s[c] : -INFINITY;
+                for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sr + c * 32));
+                tmem_wait_ld();
+                if (masked) {
+#pragma unroll
+                    for (int c = 0; c < 128; ++c) sr[c] = (c < lim) ? sr[c] : __float_as_uint(-INFINITY);
                 }
-                float mx = s[0];
+                // Row max: 3-input max in four independent chains.
+                float mx4[4] = {__uint_as_float(sr[0]), __uint_as_float(sr[1]), __uint_as_float(sr[2]),
+                                __uint_as_float(sr[3])};
 #pragma unroll
-                for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+                for (int pr = 2; pr < 64; ++pr)
+                    mx4[pr & 3] = fmax3(mx4[pr & 3], __uint_as_float(sr[2 * pr]), __uint_as_float(sr[2 * pr + 1]));
+                const float mx = fmaxf(fmax3(mx4[0], mx4[1], mx4[2]), mx4[3]);
                 const float mx_l2 = mx * p.scale_log2;
                 // Lazy rescaling: move the reference max only when it grows by more than 2^8.
                 bool need = (mx_l2 > m + kRescaleThreshold);
@@ -389,18 +474,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 const float neg_m = (m == -INFINITY) ? 0.f : -m;
-                float lsum = 0.f;
-                uint32_t pk[64];
+                const float2 scale2 = make_float2(p.scale_log2, p.scale_log2);
+                const float2 negm2 = make_float2(neg_m, neg_m);
+                float2 lsum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                // Exponentials 32 keys at a time; each chunk's 16 packed P columns are written back
+                // over S columns already read into registers.
 #pragma unroll
-                for (int c = 0; c < 64; ++c) {
-                    float p0 = ex2(fmaf(s[2 * c], p.scale_log2, neg_m));
-                    float p1 = ex2(fmaf(s[2 * c + 1], p.scale_log2, neg_m));
-                    lsum += p0 + p1;
-                    pk[c] = pack2<kBF16>(p0, p1);
+                for (int g = 0; g < 4; ++g) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int q = 0; q < 16; ++q) {
+                        const int pr = g * 16 + q;
+                        // x = s * scale * log2(e) - m, two keys per packed FMA
+                        float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[2 * pr]), __uint_as_float(sr[2 * pr + 1])),
+                                              scale2, negm2);
+                        if (!masked && poly_pair(pr)) {
+                            x = exp2_poly2(x);
+                        } else {
+                            x.x = ex2(x.x);
+                            x.y = ex2(x.y);
+                        }
+                        lsum2[q & 1] = __fadd2_rn(lsum2[q & 1], x);
+                        pk[q] = pack2<kBF16>(x.x, x.y);
+                    }
+                    tmem_st16(tS + g * 16, pk);
                 }
-                l += lsum;
-                tmem_st32(tS + 0, pk + 0);
-                tmem_st32(tS + 32, pk + 32);
+                l += (lsum2[0].x + lsum2[0].y) + (lsum2[1].x + lsum2[1].y);
                 tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&bars->p_full[wg]);

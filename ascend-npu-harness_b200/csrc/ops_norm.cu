@@ -1,28 +1,51 @@
 // layer_norm and rms_norm_rope_fused: row-wise normalisations, HBM-bound.
 //
-// A "row group" of TPR threads (8..1024, power of two) owns one row; each thread keeps VPT
-// 16-byte packs of the row in registers, so HBM sees exactly one read and one write of x.
-// A block processes RU rows per group per iteration with all loads issued before any
-// reduction, which keeps enough bytes in flight per SM to saturate HBM for short rows
-// (128-element RoPE heads) as well as long ones (4096-element LayerNorm rows).
+// Row-stream design (one persistent CTA per SM):
+//   * a producer thread copies tiles of whole consecutive rows from HBM into a ring of
+//     shared-memory stages with single bulk TMA copies (cp.async.bulk, completion on an mbarrier),
+//     keeping up to ~190 KB per SM in flight -- enough to cover HBM latency at full bandwidth
+//     without holding rows in registers;
+//   * eight consumer warps take the rows of the current stage (a group of G = 8/16/32 lanes per
+//     row), reduce the row from shared memory with shuffles, then make one more pass over the
+//     row in shared memory to normalise, apply the per-column parameters (staged in shared memory
+//     once per CTA) and, for RoPE, read the rotation partner of each element straight from the
+//     staged row; outputs leave as 16-byte streaming stores;
+//   * each consumer warp releases the stage through an mbarrier when its rows are done.
+// HBM therefore sees exactly one read and one write per element.
 //
-// Arithmetic mirrors the reference goldens step by step (explicitly rounded fp32 ops, IEEE
-// division and square root):
-//   layer_norm          ops/layer_norm/golden/layer_norm_golden.cpp:15-39 (two-pass mean/var)
+// Arithmetic mirrors the reference goldens step by step with explicitly rounded fp32 ops:
+//   layer_norm          ops/layer_norm/golden/layer_norm_golden.cpp:15-39 (two-pass mean/var,
+//                       inv_std = 1/sqrt(var+eps), y = (x-mean)*inv_std*gamma + beta)
 //   rms_norm_rope_fused ops/rms_norm_rope_fused/golden/rms_norm_rope_fused_golden.cpp:20-51
-// The goldens accumulate sums in fp64; here the sums are fp32 shuffle trees, which is the
-// only source of difference (well inside the bf16 tolerances).
+//                       (rms = sqrt(mean(x^2)+eps), y = x/rms*w, then the rotation)
+// Differences from the goldens: sums are fp32 (per-lane sequential, then a shuffle tree) instead
+// of sequential fp64, and x/rms is computed as x*(1/rms) (one extra rounding, <= 1 ulp): an IEEE
+// division per element would make the kernel instruction-bound instead of HBM-bound.
+//
+// Rows that are not a multiple of 16 bytes, or unaligned buffers, use a simple scalar kernel.
+// Waits are bounded like the tensor-core kernels'; an expired wait is reported through
+// hc_check_device_error().
 #include <cuda_runtime.h>
+
+#include <mutex>
 
 #include "hc_device.cuh"
 #include "hc_internal.h"
+#include "sm100.cuh"
 
 namespace hc {
 namespace {
 
-constexpr int kMaxVpt = 8;
+using namespace sm100;
 
 enum class NormKind { kLayerNorm, kRmsRope };
+
+constexpr uint32_t kConsumerWarps = 8;
+constexpr uint32_t kThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
+constexpr uint32_t kMaxStages = 8;
+constexpr uint32_t kSmemBudget = 200 * 1024;
+
+__device__ uint32_t g_norm_error_word;
 
 struct NormArgs {
     const void* x;
@@ -32,243 +55,300 @@ struct NormArgs {
     const float* cos_t;  // RoPE only, [S, rot/2]
     const float* sin_t;
     uint32_t rows;
-    uint32_t H;          // row length
-    uint32_t tpr;        // threads per row group
+    uint32_t H;          // row length (elements)
     float eps;
     uint32_t heads;      // rows per sequence position (RoPE)
     uint32_t S;
     uint32_t rot;        // rotary dim (even, <= H)
     uint32_t style;      // 0 interleaved, 1 rotate-half
+    uint32_t tile_rows;  // rows per shared-memory stage
+    uint32_t stages;
+    uint32_t tile_bytes;       // tile_rows * H * sizeof(T), multiple of 16
+    uint32_t param_floats;     // floats of parameters staged in shared memory
+    uint32_t param_stride;     // floats per staged parameter vector (lane-transposed, padded)
+    uint32_t vec_rope;         // 1: rotary packs never straddle the rotary boundary or the halves
 };
 
-template <int RU>
-__device__ __forceinline__ void group_reduce(float (&v)[RU], uint32_t tpr, float* red) {
-    if (tpr <= 32) {
+struct RingBars {
+    uint64_t full[kMaxStages], empty[kMaxStages];
+};
+
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
 #pragma unroll
-        for (int r = 0; r < RU; ++r)
-            for (uint32_t o = tpr >> 1; o > 0; o >>= 1) v[r] += __shfl_xor_sync(0xffffffffu, v[r], o);
-        return;
-    }
-    // tpr > 32: warp trees, then the group's warps through shared memory.
-    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t wpg = tpr >> 5;                 // warps per group
-    const uint32_t group = threadIdx.x / tpr;
-#pragma unroll
-    for (int r = 0; r < RU; ++r) {
-        float s = warp_sum(v[r]);
-        if (lane == 0) red[warp * RU + r] = s;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < RU; ++r) {
-        float s = 0.f;
-        for (uint32_t w = 0; w < wpg; ++w) s += red[(group * wpg + w) * RU + r];
-        v[r] = s;
-    }
-    __syncthreads();
+    for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
 }
 
-template <typename T, int VPT, int RU, NormKind KIND>
-__global__ void __launch_bounds__(256) rownorm_kernel(NormArgs a) {
+template <typename T>
+__device__ __forceinline__ void unpack_f(const pack<T>& p, float* f) {
+#pragma unroll
+    for (int e = 0; e < elem<T>::kPack; ++e) f[e] = elem<T>::to_f(p.v[e]);
+}
+
+// Shared-memory layout of a staged parameter vector, transposed by lane: lane gl of a row group
+// always handles packs k = gl + G*i, so the four parameters of quad q of pack k are stored at
+// float index ((i * P/4 + q) * G + gl) * 4.  Consecutive lanes then read consecutive 16-byte
+// slots (no bank conflicts), where the natural layout would put them 4*P bytes apart.
+template <int P, int G>
+__device__ __forceinline__ uint32_t param_slot(uint32_t k, uint32_t q) {
+    return ((k / G * (P / 4) + q) * G + k % G) * 4;
+}
+
+template <int P, int G>
+__device__ __forceinline__ void load_params(const float* base, uint32_t k, float* out) {
+#pragma unroll
+    for (int q = 0; q < P / 4; ++q) {
+        const float4 v = *reinterpret_cast<const float4*>(base + param_slot<P, G>(k, q));
+        out[4 * q] = v.x; out[4 * q + 1] = v.y; out[4 * q + 2] = v.z; out[4 * q + 3] = v.w;
+    }
+}
+
+template <int N>
+__device__ __forceinline__ void ldg_f32(const float* p, float* out) {
+    if (N % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < N; i += 4) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(p + i));
+            out[i] = v.x; out[i + 1] = v.y; out[i + 2] = v.z; out[i + 3] = v.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < N; i += 2) {
+            const float2 v = __ldg(reinterpret_cast<const float2*>(p + i));
+            out[i] = v.x; out[i + 1] = v.y;
+        }
+    }
+}
+
+// Processes one row held in shared memory with the G lanes of a row group.  Every lane of the warp
+// calls it the same number of times (the shuffles use the full mask); groups without a row of
+// their own pass valid = false and only take part in the shuffles.
+template <typename T, NormKind KIND, int G>
+__device__ __forceinline__ void process_row(const NormArgs& a, const pack<T>* srow, const float* params, uint64_t row,
+                                            uint32_t gl, bool valid) {
     constexpr int P = elem<T>::kPack;
-    extern __shared__ float smem[];
-    float* red = smem;                                   // (blockDim/32) * RU floats
-    float* rope_buf = smem + (blockDim.x / 32) * RU;     // groups * RU * H floats (rotate-half only)
-
-    const uint32_t tpr = a.tpr;
-    const uint32_t groups = blockDim.x / tpr;
-    const uint32_t group = threadIdx.x / tpr;
-    const uint32_t gl = threadIdx.x % tpr;                 // lane within group
-    const uint32_t packs = a.H / P;
-    const uint64_t rows_per_iter = static_cast<uint64_t>(groups) * RU;
-    const T* x = static_cast<const T*>(a.x);
-    T* y = static_cast<T*>(a.y);
-    const float inv_h = 1.0f / static_cast<float>(a.H);
-    (void)inv_h;
-
-    for (uint64_t base = static_cast<uint64_t>(blockIdx.x) * rows_per_iter; base < a.rows;
-         base += static_cast<uint64_t>(gridDim.x) * rows_per_iter) {
-        float xv[RU][VPT][P];
-        // ---- loads (all rows of this iteration first) ----
+    const uint32_t packs = valid ? a.H / P : 0u;
+    const float invH = 1.0f / static_cast<float>(a.H);
+    (void)invH;
+    // ---- pass 1 (and 2 for LayerNorm): statistics from shared memory ----
+    float s = 0.f;
+    for (uint32_t k = gl; k < packs; k += G) {
+        float f[P];
+        unpack_f<T>(srow[k], f);
 #pragma unroll
-        for (int r = 0; r < RU; ++r) {
-            uint64_t row = base + group * RU + r;
+        for (int e = 0; e < P; ++e) s = (KIND == NormKind::kLayerNorm) ? __fadd_rn(s, f[e]) : __fadd_rn(s, __fmul_rn(f[e], f[e]));
+    }
+    s = group_sum<G>(s);
+    float mul, sub = 0.f;
+    if (KIND == NormKind::kLayerNorm) {
+        const float mean = __fdiv_rn(s, static_cast<float>(a.H));
+        float q = 0.f;
+        for (uint32_t k = gl; k < packs; k += G) {
+            float f[P];
+            unpack_f<T>(srow[k], f);
 #pragma unroll
-            for (int v = 0; v < VPT; ++v) {
-                uint32_t pi = v * tpr + gl;
-                if (row < a.rows && pi < packs) {
-                    pack<T> pk = ld_stream(reinterpret_cast<const pack<T>*>(x + row * a.H) + pi);
-#pragma unroll
-                    for (int e = 0; e < P; ++e) xv[r][v][e] = elem<T>::to_f(pk.v[e]);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < P; ++e) xv[r][v][e] = 0.f;
-                }
+            for (int e = 0; e < P; ++e) {
+                const float d = __fsub_rn(f[e], mean);
+                q = __fadd_rn(q, __fmul_rn(d, d));
             }
         }
-        float scale_a[RU], shift_a[RU];
+        q = group_sum<G>(q);
+        mul = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(q, static_cast<float>(a.H)), a.eps)));  // inv_std
+        sub = mean;
+    } else {
+        mul = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, static_cast<float>(a.H)), a.eps)));  // 1/rms
+    }
+    // ---- last pass: normalise (+ RoPE) and store ----
+    if (!valid) return;
+    T* yrow = static_cast<T*>(a.y) + row * a.H;
+    const uint32_t half = a.rot / 2;
+    const float* cs = nullptr;
+    const float* sn = nullptr;
+    if (KIND == NormKind::kRmsRope) {
+        const uint32_t s_pos = static_cast<uint32_t>((row / a.heads) % a.S);
+        cs = a.cos_t + static_cast<size_t>(s_pos) * half;
+        sn = a.sin_t + static_cast<size_t>(s_pos) * half;
+    }
+    for (uint32_t k = gl; k < packs; k += G) {
+        const uint32_t d0 = k * P;
+        float f[P], g[P];
+        unpack_f<T>(srow[k], f);
+        load_params<P, G>(params, k, g);
+        float out[P];
         if (KIND == NormKind::kLayerNorm) {
-            float s[RU];
+            float b[P];
+            load_params<P, G>(params + a.param_stride, k, b);
 #pragma unroll
-            for (int r = 0; r < RU; ++r) {
-                s[r] = 0.f;
-#pragma unroll
-                for (int v = 0; v < VPT; ++v)
-#pragma unroll
-                    for (int e = 0; e < P; ++e) s[r] += xv[r][v][e];
-            }
-            group_reduce<RU>(s, tpr, red);
-            float mean[RU];
-#pragma unroll
-            for (int r = 0; r < RU; ++r) mean[r] = __fdiv_rn(s[r], static_cast<float>(a.H));
-#pragma unroll
-            for (int r = 0; r < RU; ++r) {
-                s[r] = 0.f;
-#pragma unroll
-                for (int v = 0; v < VPT; ++v) {
-                    uint32_t pi = v * tpr + gl;
-                    if (pi < packs) {
-#pragma unroll
-                        for (int e = 0; e < P; ++e) {
-                            float d = __fsub_rn(xv[r][v][e], mean[r]);
-                            s[r] = __fadd_rn(s[r], __fmul_rn(d, d));
-                        }
-                    }
-                }
-            }
-            group_reduce<RU>(s, tpr, red);
-#pragma unroll
-            for (int r = 0; r < RU; ++r) {
-                float var = __fdiv_rn(s[r], static_cast<float>(a.H));
-                scale_a[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));  // inv_std
-                shift_a[r] = mean[r];
+            for (int e = 0; e < P; ++e) {
+                const float nrm = __fmul_rn(__fsub_rn(f[e], sub), mul);
+                out[e] = __fadd_rn(__fmul_rn(nrm, g[e]), b[e]);
             }
         } else {
-            float s[RU];
 #pragma unroll
-            for (int r = 0; r < RU; ++r) {
-                s[r] = 0.f;
+            for (int e = 0; e < P; ++e) out[e] = __fmul_rn(__fmul_rn(f[e], mul), g[e]);
+            if (a.vec_rope && d0 < a.rot) {
+                // Whole pack inside the rotary part, tables read as vectors.
+                if (a.style == 0) {
+                    float c[P / 2], z[P / 2];
+                    ldg_f32<P / 2>(cs + d0 / 2, c);
+                    ldg_f32<P / 2>(sn + d0 / 2, z);
 #pragma unroll
-                for (int v = 0; v < VPT; ++v)
-#pragma unroll
-                    for (int e = 0; e < P; ++e) s[r] = __fadd_rn(s[r], __fmul_rn(xv[r][v][e], xv[r][v][e]));
-            }
-            group_reduce<RU>(s, tpr, red);
-#pragma unroll
-            for (int r = 0; r < RU; ++r) {
-                scale_a[r] = __fsqrt_rn(__fadd_rn(__fdiv_rn(s[r], static_cast<float>(a.H)), a.eps));  // rms
-                shift_a[r] = 0.f;
-            }
-        }
-
-        // ---- normalise ----
-#pragma unroll
-        for (int r = 0; r < RU; ++r) {
-#pragma unroll
-            for (int v = 0; v < VPT; ++v) {
-                uint32_t pi = v * tpr + gl;
-                if (pi >= packs) continue;
-                uint32_t e0 = pi * P;
-#pragma unroll
-                for (int e = 0; e < P; ++e) {
-                    float g = __ldg(a.gamma + e0 + e);
-                    if (KIND == NormKind::kLayerNorm) {
-                        float nrm = __fmul_rn(__fsub_rn(xv[r][v][e], shift_a[r]), scale_a[r]);
-                        xv[r][v][e] = __fadd_rn(__fmul_rn(nrm, g), __ldg(a.beta + e0 + e));
-                    } else {
-                        xv[r][v][e] = __fmul_rn(__fdiv_rn(xv[r][v][e], scale_a[r]), g);
+                    for (int e = 0; e < P; e += 2) {
+                        const float ye = out[e], yo = out[e + 1];
+                        out[e] = __fsub_rn(__fmul_rn(ye, c[e / 2]), __fmul_rn(yo, z[e / 2]));
+                        out[e + 1] = __fadd_rn(__fmul_rn(ye, z[e / 2]), __fmul_rn(yo, c[e / 2]));
                     }
-                }
-            }
-        }
-
-        // ---- RoPE ----
-        if (KIND == NormKind::kRmsRope && a.rot > 0) {
-            const uint32_t half = a.rot / 2;
-            if (a.style == 1) {
-                // Rotate-half pairs (d, d + half) may live in different threads: exchange the
-                // normalised row through shared memory.
-#pragma unroll
-                for (int r = 0; r < RU; ++r) {
-                    float* buf = rope_buf + (static_cast<size_t>(group) * RU + r) * a.H;
-#pragma unroll
-                    for (int v = 0; v < VPT; ++v) {
-                        uint32_t pi = v * tpr + gl;
-                        if (pi >= packs) continue;
-#pragma unroll
-                        for (int e = 0; e < P; ++e) buf[pi * P + e] = xv[r][v][e];
-                    }
-                }
-                if (tpr <= 32) __syncwarp(); else __syncthreads();
-                // For tpr < 32 several groups share a warp; __syncwarp covers all of them.
-            }
-#pragma unroll
-            for (int r = 0; r < RU; ++r) {
-                uint64_t row = base + group * RU + r;
-                if (row >= a.rows) continue;
-                uint32_t s_pos = static_cast<uint32_t>((row / a.heads) % a.S);
-                const float* cs = a.cos_t + static_cast<size_t>(s_pos) * half;
-                const float* sn = a.sin_t + static_cast<size_t>(s_pos) * half;
-                const float* buf = rope_buf + (static_cast<size_t>(group) * RU + r) * a.H;
-#pragma unroll
-                for (int v = 0; v < VPT; ++v) {
-                    uint32_t pi = v * tpr + gl;
-                    if (pi >= packs) continue;
-                    float outv[P];
+                } else {
+                    const bool first = d0 < half;
+                    const uint32_t kp = first ? k + half / P : k - half / P;  // partner pack
+                    float fp[P], gp[P], c[P], z[P];
+                    unpack_f<T>(srow[kp], fp);
+                    load_params<P, G>(params, kp, gp);
+                    ldg_f32<P>(cs + (first ? d0 : d0 - half), c);
+                    ldg_f32<P>(sn + (first ? d0 : d0 - half), z);
 #pragma unroll
                     for (int e = 0; e < P; ++e) {
-                        uint32_t d = pi * P + e;
-                        float val = xv[r][v][e];
-                        if (d < a.rot) {
-                            if (a.style == 0) {
-                                uint32_t i = d >> 1;
-                                float c = __ldg(cs + i), z = __ldg(sn + i);
-                                // pair partner sits in the same pack (P is even)
-                                float other = (e & 1) ? xv[r][v][e - 1] : xv[r][v][e + 1];
-                                if ((d & 1) == 0) val = __fsub_rn(__fmul_rn(val, c), __fmul_rn(other, z));
-                                else val = __fadd_rn(__fmul_rn(other, z), __fmul_rn(val, c));
-                            } else {
-                                if (d < half) {
-                                    float c = __ldg(cs + d), z = __ldg(sn + d);
-                                    val = __fsub_rn(__fmul_rn(val, c), __fmul_rn(buf[d + half], z));
-                                } else {
-                                    uint32_t i = d - half;
-                                    float c = __ldg(cs + i), z = __ldg(sn + i);
-                                    val = __fadd_rn(__fmul_rn(buf[i], z), __fmul_rn(val, c));
-                                }
-                            }
-                        }
-                        outv[e] = val;
+                        const float partner = __fmul_rn(__fmul_rn(fp[e], mul), gp[e]);
+                        out[e] = first ? __fsub_rn(__fmul_rn(out[e], c[e]), __fmul_rn(partner, z[e]))
+                                       : __fadd_rn(__fmul_rn(partner, z[e]), __fmul_rn(out[e], c[e]));
                     }
+                }
+            } else if (d0 < a.rot) {
+                if (a.style == 0) {
+                    // interleaved pairs (2i, 2i+1); a pack starts on an even column
 #pragma unroll
-                    for (int e = 0; e < P; ++e) xv[r][v][e] = outv[e];
+                    for (int e = 0; e < P; e += 2) {
+                        const uint32_t d = d0 + e;
+                        if (d < a.rot) {
+                            const float c = __ldg(cs + d / 2), z = __ldg(sn + d / 2);
+                            const float ye = out[e], yo = out[e + 1];
+                            out[e] = __fsub_rn(__fmul_rn(ye, c), __fmul_rn(yo, z));
+                            out[e + 1] = __fadd_rn(__fmul_rn(ye, z), __fmul_rn(yo, c));
+                        }
+                    }
+                } else {
+                    // rotate-half pairs (d, d + half): the partner is read from the staged row
+                    const T* xs = reinterpret_cast<const T*>(srow);
+#pragma unroll
+                    for (int e = 0; e < P; ++e) {
+                        const uint32_t d = d0 + e;
+                        if (d < a.rot) {
+                            const bool first = d < half;
+                            const uint32_t i = first ? d : d - half;
+                            const uint32_t pd = first ? d + half : d - half;
+                            const float wp = params[param_slot<P, G>(pd / P, (pd % P) / 4) + pd % 4];
+                            const float partner = __fmul_rn(__fmul_rn(elem<T>::to_f(xs[pd]), mul), wp);
+                            const float c = __ldg(cs + i), z = __ldg(sn + i);
+                            out[e] = first ? __fsub_rn(__fmul_rn(out[e], c), __fmul_rn(partner, z))
+                                           : __fadd_rn(__fmul_rn(partner, z), __fmul_rn(out[e], c));
+                        }
+                    }
                 }
             }
-            if (a.style == 1) {
-                if (tpr <= 32) __syncwarp(); else __syncthreads();
-            }
         }
-
-        // ---- stores ----
+        pack<T> o;
 #pragma unroll
-        for (int r = 0; r < RU; ++r) {
-            uint64_t row = base + group * RU + r;
-            if (row >= a.rows) continue;
-#pragma unroll
-            for (int v = 0; v < VPT; ++v) {
-                uint32_t pi = v * tpr + gl;
-                if (pi >= packs) continue;
-                pack<T> pk;
-#pragma unroll
-                for (int e = 0; e < P; ++e) pk.v[e] = elem<T>::from_f(xv[r][v][e]);
-                st_stream(reinterpret_cast<pack<T>*>(y + row * a.H) + pi, pk);
-            }
-        }
+        for (int e = 0; e < P; ++e) o.v[e] = elem<T>::from_f(out[e]);
+        st_stream(reinterpret_cast<pack<T>*>(yrow) + k, o);
     }
 }
 
-// Scalar fallback (unaligned buffers or rows not a multiple of the pack): one block per row,
-// three passes over the row (the row stays in L1/L2 between passes).
+template <typename T, NormKind KIND, int G>
+__global__ void __launch_bounds__(kThreads, 1) rowstream_kernel(NormArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    float* params = reinterpret_cast<float*>(smem);
+    uint8_t* ring = smem + ((a.param_floats * 4 + 127) & ~127u);
+    RingBars* bars = reinterpret_cast<RingBars*>(ring + a.stages * a.tile_bytes);
+    volatile uint32_t* abort_flag = reinterpret_cast<uint32_t*>(bars + 1);
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const uint64_t num_tiles = (a.rows + a.tile_rows - 1) / a.tile_rows;
+    const size_t row_bytes = static_cast<size_t>(a.H) * sizeof(T);
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < a.stages; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], kConsumerWarps);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    // Stage the per-column parameters once per CTA, lane-transposed (see param_slot).
+    {
+        constexpr uint32_t P = elem<T>::kPack;
+        for (uint32_t i = threadIdx.x; i < a.H; i += blockDim.x) {
+            const uint32_t slot = param_slot<P, G>(i / P, (i % P) / 4) + i % 4;
+            params[slot] = a.gamma[i];
+            if (KIND == NormKind::kLayerNorm) params[a.param_stride + slot] = a.beta[i];
+        }
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ================================ producer ================================
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, pend_valid = 0, pend_phase = 0;
+            bool ok = true;
+            for (uint64_t t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+                if (!mbar_wait_bounded(&bars->empty[stage], phase ^ 1, abort_flag, &g_norm_error_word, 1u)) {
+                    ok = false;
+                    break;
+                }
+                const uint64_t r0 = t * a.tile_rows;
+                const uint64_t nr = (a.rows - r0 < a.tile_rows) ? (a.rows - r0) : a.tile_rows;
+                const uint32_t bytes = static_cast<uint32_t>(nr * row_bytes);
+                mbar_arrive_expect_tx(&bars->full[stage], bytes);
+                asm volatile(
+                    "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                        smem_u32(ring + stage * a.tile_bytes)),
+                    "l"(static_cast<const uint8_t*>(a.x) + r0 * row_bytes), "r"(bytes), "r"(smem_u32(&bars->full[stage]))
+                    : "memory");
+                pend_valid |= 1u << stage;
+                pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
+                if (++stage == a.stages) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            if (!ok) {  // drain copies still in flight before the CTA's shared memory goes away
+                volatile uint32_t never = 0;
+                for (uint32_t s = 0; s < a.stages; ++s)
+                    if (pend_valid & (1u << s))
+                        mbar_wait_bounded(&bars->full[s], (pend_phase >> s) & 1u, &never, &g_norm_error_word, 4u,
+                                          1000000000ull);
+            }
+        }
+    } else {
+        // ================================ consumers ================================
+        constexpr uint32_t kRowsPerPass = 32 / G;
+        const uint32_t sub = lane / G, gl = lane % G;
+        uint32_t stage = 0, phase = 0;
+        for (uint64_t t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+            bool ok = mbar_wait_bounded(&bars->full[stage], phase, abort_flag, &g_norm_error_word, 2u);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const uint64_t r0 = t * a.tile_rows;
+            const uint32_t nr = static_cast<uint32_t>((a.rows - r0 < a.tile_rows) ? (a.rows - r0) : a.tile_rows);
+            const uint8_t* tile = ring + stage * a.tile_bytes;
+            for (uint32_t rb = warp * kRowsPerPass; rb < nr; rb += kConsumerWarps * kRowsPerPass) {
+                const uint32_t rr = rb + sub;
+                const bool valid = rr < nr;
+                process_row<T, KIND, G>(a, reinterpret_cast<const pack<T>*>(tile + (valid ? rr : rb) * row_bytes),
+                                        params, r0 + rr, gl, valid);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->empty[stage]);
+            if (++stage == a.stages) {
+                stage = 0;
+                phase ^= 1;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// Scalar fallback (unaligned buffers or rows that are not a multiple of 16 bytes): one block per
+// row, three passes over the row staged in shared memory.
 template <typename T, NormKind KIND>
 __global__ void __launch_bounds__(256) rownorm_scalar_kernel(NormArgs a) {
     __shared__ float red[8];
@@ -293,7 +373,7 @@ __global__ void __launch_bounds__(256) rownorm_scalar_kernel(NormArgs a) {
             return t;
         };
         s = block_sum(s);
-        float scale, shift = 0.f;
+        float mul, shift = 0.f;
         if (KIND == NormKind::kLayerNorm) {
             float mean = __fdiv_rn(s, static_cast<float>(a.H));
             float q = 0.f;
@@ -302,17 +382,17 @@ __global__ void __launch_bounds__(256) rownorm_scalar_kernel(NormArgs a) {
                 q = __fadd_rn(q, __fmul_rn(dd, dd));
             }
             q = block_sum(q);
-            scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(q, static_cast<float>(a.H)), a.eps)));
+            mul = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(q, static_cast<float>(a.H)), a.eps)));
             shift = mean;
         } else {
-            scale = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, static_cast<float>(a.H)), a.eps));
+            mul = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, static_cast<float>(a.H)), a.eps)));
         }
         for (uint32_t d = threadIdx.x; d < a.H; d += blockDim.x) {
             float v = row_buf[d];
             if (KIND == NormKind::kLayerNorm)
-                v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, shift), scale), a.gamma[d]), a.beta[d]);
+                v = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(v, shift), mul), a.gamma[d]), a.beta[d]);
             else
-                v = __fmul_rn(__fdiv_rn(v, scale), a.gamma[d]);
+                v = __fmul_rn(__fmul_rn(v, mul), a.gamma[d]);
             row_buf[d] = v;
         }
         __syncthreads();
@@ -338,27 +418,62 @@ __global__ void __launch_bounds__(256) rownorm_scalar_kernel(NormArgs a) {
     }
 }
 
-uint32_t next_pow2(uint32_t v) {
-    uint32_t p = 1;
-    while (p < v) p <<= 1;
-    return p;
+uint32_t read_error_word(const char** name) {
+    *name = "layer_norm/rms_norm_rope_fused row stream";
+    uint32_t word = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&word, g_norm_error_word, sizeof(word)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (word) cudaMemcpyToSymbol(g_norm_error_word, &zero, sizeof(zero));
+    return word;
 }
 
-template <typename T, int VPT, NormKind KIND>
-int launch_rownorm_vec(NormArgs a, uint32_t threads, cudaStream_t s) {
-    constexpr int RU = (VPT <= 2) ? 2 : 1;
-    uint32_t groups = threads / a.tpr;
-    size_t smem = (threads / 32) * RU * sizeof(float);
-    if (KIND == NormKind::kRmsRope && a.style == 1) smem += static_cast<size_t>(groups) * RU * a.H * sizeof(float);
-    if (smem > 48 * 1024) {
-        if (cudaFuncSetAttribute(rownorm_kernel<T, VPT, RU, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem)) != cudaSuccess)
-            return cuda_fail(cudaGetLastError(), "cudaFuncSetAttribute(rownorm)");
+template <typename T, NormKind KIND, int G>
+int launch_rowstream(NormArgs a, cudaStream_t s) {
+    static std::once_flag reg_once;
+    std::call_once(reg_once, [] { register_error_word(read_error_word); });
+    constexpr uint32_t P = elem<T>::kPack;
+    const uint32_t packs = a.H / P;
+    a.param_stride = (packs + G - 1) / G * G * P;
+    a.param_floats = (KIND == NormKind::kLayerNorm ? 2 : 1) * a.param_stride;
+    if (a.param_floats * 4ull > 64 * 1024) return fail(HC_ERR_UNSUPPORTED, "row of %u elements too long", a.H);
+    a.vec_rope = (KIND == NormKind::kRmsRope) && a.rot % P == 0 && (a.rot / 2) % P == 0 &&
+                 (a.rot / 2) % 4 == 0 && aligned16(a.cos_t) && aligned16(a.sin_t);
+    const uint32_t row_bytes = a.H * static_cast<uint32_t>(sizeof(T));
+    const uint32_t rows_per_pass = kConsumerWarps * (32 / G);
+    const uint32_t param_bytes = ((a.param_floats * 4 + 127) & ~127u);
+    // Tile: whole passes of the consumer warps, 16..64 KB when rows allow.
+    uint32_t passes = 1;
+    while (passes < 64 && rows_per_pass * (passes * 2) * row_bytes <= 32 * 1024) passes *= 2;
+    a.tile_rows = rows_per_pass * passes;
+    if (static_cast<uint64_t>(a.tile_rows) * row_bytes > 64 * 1024) {
+        a.tile_rows = (64 * 1024) / row_bytes;
+        if (a.tile_rows == 0) a.tile_rows = 1;
     }
-    uint64_t iters = (a.rows + static_cast<uint64_t>(groups) * RU - 1) / (static_cast<uint64_t>(groups) * RU);
-    uint64_t cap = static_cast<uint64_t>(sm_count()) * (2048 / threads);
-    int blocks = static_cast<int>(iters < cap ? iters : cap);
-    rownorm_kernel<T, VPT, RU, KIND><<<blocks, threads, smem, s>>>(a);
+    a.tile_bytes = a.tile_rows * row_bytes;
+    const uint32_t bar_bytes = sizeof(RingBars) + 16;
+    uint32_t avail = kSmemBudget - param_bytes - bar_bytes - 128;
+    a.stages = avail / a.tile_bytes;
+    if (a.stages > kMaxStages) a.stages = kMaxStages;
+    if (a.stages < 2) {
+        a.tile_rows = 1;
+        a.tile_bytes = row_bytes;
+        a.stages = avail / a.tile_bytes;
+        if (a.stages > kMaxStages) a.stages = kMaxStages;
+        if (a.stages < 2) return fail(HC_ERR_UNSUPPORTED, "row of %u bytes too long for the row-stream kernel", row_bytes);
+    }
+    const size_t smem = 128 + param_bytes + static_cast<size_t>(a.stages) * a.tile_bytes + bar_bytes;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(rowstream_kernel<T, KIND, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kSmemBudget + 1024));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowstream_kernel)");
+        attr_set = true;
+    }
+    const uint64_t tiles = (a.rows + a.tile_rows - 1) / a.tile_rows;
+    const uint64_t grid = tiles < static_cast<uint64_t>(sm_count()) ? tiles : static_cast<uint64_t>(sm_count());
+    rowstream_kernel<T, KIND, G><<<static_cast<unsigned>(grid), kThreads, smem, s>>>(a);
     return check_launch(KIND == NormKind::kLayerNorm ? "layer_norm" : "rms_norm_rope_fused");
 }
 
@@ -366,24 +481,14 @@ template <typename T, NormKind KIND>
 int launch_rownorm(NormArgs a, void* stream) {
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     constexpr uint32_t P = elem<T>::kPack;
+    a.param_floats = (KIND == NormKind::kLayerNorm ? 2 : 1) * a.H;
     const uint32_t packs = a.H / P;
-    bool vec = (a.H % P == 0) && aligned16(a.x) && aligned16(a.y) && packs <= 1024 * kMaxVpt;
-    if (vec) {
-        // Aim for 4 packs per thread; groups of at least 8 threads (tiny rows) and at most 1024.
-        uint32_t tpr = next_pow2((packs + 3) / 4);
-        if (tpr < 8) tpr = 8;
-        if (tpr > 1024) tpr = 1024;
-        uint32_t vpt = next_pow2((packs + tpr - 1) / tpr);
-        if (vpt == 0) vpt = 1;
-        a.tpr = tpr;
-        uint32_t threads = tpr < 256 ? 256 : tpr;
-        switch (vpt) {
-            case 1: return launch_rownorm_vec<T, 1, KIND>(a, threads, s);
-            case 2: return launch_rownorm_vec<T, 2, KIND>(a, threads, s);
-            case 4: return launch_rownorm_vec<T, 4, KIND>(a, threads, s);
-            case 8: return launch_rownorm_vec<T, 8, KIND>(a, threads, s);
-            default: break;
-        }
+    const bool stream_ok = (a.H % P == 0) && aligned16(a.x) && aligned16(a.y) &&
+                           a.param_floats * 4ull <= 64 * 1024;
+    if (stream_ok) {
+        if (packs >= 32) return launch_rowstream<T, KIND, 32>(a, s);
+        if (packs >= 16) return launch_rowstream<T, KIND, 16>(a, s);
+        return launch_rowstream<T, KIND, 8>(a, s);
     }
     size_t smem = static_cast<size_t>(a.H) * sizeof(float);
     if (smem > 200 * 1024) return fail(HC_ERR_UNSUPPORTED, "row length %u too long for the scalar row kernel", a.H);

@@ -385,11 +385,16 @@ def run_ours(args):
     d.close()
 
 
-def run_extras(hc, d: Dist, dev, peaks, args) -> dict:
+EXTRA_OPS = ("flash_attention_fwd_noncausal", "matmul_bias", "layer_norm", "rms_norm_rope_fused", "elementwise_add")
+
+
+def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
     """The other BASELINE configurations, each timed alone (W=3, 20 launches)."""
     import torch
 
     out = {}
+    if not want:
+        return out
     steps, warm = 20, 3
     flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     flush = lambda: flush_buf.zero_()  # noqa: E731  (256 MB > 126 MB L2)
@@ -402,61 +407,83 @@ def run_extras(hc, d: Dist, dev, peaks, args) -> dict:
                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                                   "algorithmic_bytes_per_launch": bytes_, "traffic": profile_traffic(name)}}
 
-    # non-causal attention, same shapes
-    q, k, v = (torch.randn((FA_B, FA_H, FA_S, FA_D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
-    o = torch.empty_like(q)
-    lse = torch.empty((FA_B, FA_H, FA_S), dtype=torch.float32, device=dev)
-    ms = time_launches(lambda: hc.flash_attention_fwd(q, k, v, False, out=o, lse=lse), 5, 2, d)
-    fl = fa_flops(FA_B, FA_H, FA_S, FA_S, FA_D, False)
-    tf = fl / (ms * 1e-3) / 1e12
-    out["flash_attention_fwd_noncausal"] = {"value": d.world * tf, "unit": "TFLOP/s", "per_gpu": tf, "ms": ms,
-                                            "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"],
-                                                         "unit": "TFLOP/s", "frac": tf / peaks["bf16_tflops"]}}
-    del q, k, v, o, lse
+    if "flash_attention_fwd_noncausal" in want:  # same shapes as the headline, no mask
+        q, k, v = (torch.randn((FA_B, FA_H, FA_S, FA_D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+        o = torch.empty_like(q)
+        lse = torch.empty((FA_B, FA_H, FA_S), dtype=torch.float32, device=dev)
+        ms = time_launches(lambda: hc.flash_attention_fwd(q, k, v, False, out=o, lse=lse), 5, warm, d)
+        fl = fa_flops(FA_B, FA_H, FA_S, FA_S, FA_D, False)
+        tf = fl / (ms * 1e-3) / 1e12
+        out["flash_attention_fwd_noncausal"] = {
+            "value": d.world * tf, "unit": "TFLOP/s", "per_gpu": tf, "ms": ms,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": tf / peaks["bf16_tflops"], "algorithmic_flops_per_launch": fl}}
+        del q, k, v, o, lse
 
-    # matmul_bias 8192^3 bf16
-    M = K = N = 8192
-    A = (torch.randn((M, K), generator=g, device=dev) / math.sqrt(K)).to(torch.bfloat16)
-    B = (torch.randn((K, N), generator=g, device=dev) / math.sqrt(K)).to(torch.bfloat16)
-    bias = (torch.randn((N,), generator=g, device=dev) * 0.1).to(torch.bfloat16)
-    C = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
-    ms = time_launches(lambda: hc.matmul_bias(A, B, bias, out=C), steps, warm, d)
-    tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
-    out["matmul_bias"] = {"value": d.world * tf, "unit": "TFLOP/s", "per_gpu": tf, "ms": ms,
-                          "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                                       "frac": tf / peaks["bf16_tflops"]}}
-    del A, B, bias, C
+    if "matmul_bias" in want:  # 8192^3 bf16, A, B ~ N(0,1)/sqrt(K), bias ~ N(0, 0.1)
+        M = K = N = 8192
+        A = (torch.randn((M, K), generator=g, device=dev) / math.sqrt(K)).to(torch.bfloat16)
+        B = (torch.randn((K, N), generator=g, device=dev) / math.sqrt(K)).to(torch.bfloat16)
+        bias = (torch.randn((N,), generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        C = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        ms = time_launches(lambda: hc.matmul_bias(A, B, bias, out=C), steps, warm, d)
+        fl = 2.0 * M * N * K
+        tf = fl / (ms * 1e-3) / 1e12
+        out["matmul_bias"] = {"value": d.world * tf, "unit": "TFLOP/s", "per_gpu": tf, "ms": ms,
+                              "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"],
+                                           "unit": "TFLOP/s", "frac": tf / peaks["bf16_tflops"],
+                                           "algorithmic_flops_per_launch": fl}}
+        del A, B, bias, C
 
-    # layer_norm [16384, 4096] bf16
-    x = torch.randn((16384, 4096), generator=g, device=dev).to(torch.bfloat16)
-    gamma = torch.rand((4096,), generator=g, device=dev) + 0.5
-    beta = torch.rand((4096,), generator=g, device=dev) * 0.2 - 0.1
-    y = torch.empty_like(x)
-    ms = time_launches(lambda: hc.layer_norm(x, gamma, beta, 1e-5, y=y), steps, warm, d, flush=flush)
-    bw_entry("layer_norm", 2 * x.numel() * 2 + 2 * 4096 * 4, ms)
-    del x, y
+    if "layer_norm" in want:  # [16384, 4096] bf16, fp32 gamma/beta
+        x = torch.randn((16384, 4096), generator=g, device=dev).to(torch.bfloat16)
+        gamma = torch.rand((4096,), generator=g, device=dev) + 0.5
+        beta = torch.rand((4096,), generator=g, device=dev) * 0.2 - 0.1
+        y = torch.empty_like(x)
+        ms = time_launches(lambda: hc.layer_norm(x, gamma, beta, 1e-5, y=y), steps, warm, d, flush=flush)
+        bw_entry("layer_norm", 2 * x.numel() * 2 + 2 * 4096 * 4, ms)
+        del x, y
 
-    # rms_norm_rope_fused [8, 4096, 32, 128] bf16, rotate-half
-    x = torch.randn((8, 4096, 32, 128), generator=g, device=dev).to(torch.bfloat16)
-    w = torch.rand((128,), generator=g, device=dev) + 0.5
-    pos = torch.arange(4096, device=dev, dtype=torch.float32)[:, None]
-    inv = 1.0 / (10000.0 ** (torch.arange(64, device=dev, dtype=torch.float32) * 2 / 128))
-    cos, sin = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
-    y = torch.empty_like(x)
-    ms = time_launches(lambda: hc.rms_norm_rope_fused(x, w, cos, sin, 128, 1e-6, heads=32, rope_style=1, out=y),
-                       steps, warm, d, flush=flush)
-    bw_entry("rms_norm_rope_fused", 2 * x.numel() * 2 + 128 * 4 + 2 * cos.numel() * 4, ms)
-    del x, y
+    if "rms_norm_rope_fused" in want:  # [8, 4096, 32, 128] bf16, rotate-half, fp32 cos/sin [4096, 64]
+        x = torch.randn((8, 4096, 32, 128), generator=g, device=dev).to(torch.bfloat16)
+        w = torch.rand((128,), generator=g, device=dev) + 0.5
+        pos = torch.arange(4096, device=dev, dtype=torch.float32)[:, None]
+        inv = 1.0 / (10000.0 ** (torch.arange(64, device=dev, dtype=torch.float32) * 2 / 128))
+        cos, sin = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
+        y = torch.empty_like(x)
+        ms = time_launches(lambda: hc.rms_norm_rope_fused(x, w, cos, sin, 128, 1e-6, heads=32, rope_style=1, out=y),
+                           steps, warm, d, flush=flush)
+        bw_entry("rms_norm_rope_fused", 2 * x.numel() * 2 + 128 * 4 + 2 * cos.numel() * 4, ms)
+        del x, y
 
-    # elementwise_add fp16 [4096, 8192]
-    a = (torch.rand((4096, 8192), generator=g, device=dev) * 2 - 1).to(torch.float16)
-    b = (torch.rand((4096, 8192), generator=g, device=dev) * 2 - 1).to(torch.float16)
-    z = torch.empty_like(a)
-    ms = time_launches(lambda: hc.elementwise_add(a, b, z), steps, warm, d, flush=flush)
-    bw_entry("elementwise_add", 3 * a.numel() * 2, ms)
-    del a, b, z, flush_buf
+    if "elementwise_add" in want:  # fp16 [4096, 8192], U[-1, 1]
+        a = (torch.rand((4096, 8192), generator=g, device=dev) * 2 - 1).to(torch.float16)
+        b = (torch.rand((4096, 8192), generator=g, device=dev) * 2 - 1).to(torch.float16)
+        z = torch.empty_like(a)
+        ms = time_launches(lambda: hc.elementwise_add(a, b, z), steps, warm, d, flush=flush)
+        bw_entry("elementwise_add", 3 * a.numel() * 2, ms)
+        del a, b, z
+    del flush_buf
     torch.cuda.empty_cache()
     return out
+
+
+def run_only(args):
+    """One non-headline configuration alone (used for per-kernel profiling captures)."""
+    import torch
+
+    d = Dist(args.gpus)
+    dev = torch.device("cuda", d.local)
+    torch.cuda.set_device(dev)
+    import hc
+
+    hc.load()
+    peaks, _ = load_peaks()
+    out = run_extras(hc, d, dev, peaks, args, want=(args.only,))
+    hc.check_device_error()
+    if d.rank == 0:
+        print(json.dumps({"only": args.only, **out[args.only]}), flush=True)
+    d.close()
 
 
 def main():
@@ -470,11 +497,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--fa-batch", type=int, default=FA_B,
                     help="attention batch per GPU (default 16, the BASELINE size; smaller only for profiling captures)")
+    ap.add_argument("--only", choices=EXTRA_OPS, default=None,
+                    help="time one non-headline configuration alone and print its entry (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 untimed warm-up steps
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.only:
+        run_only(args)
     else:
         run_ours(args)
 

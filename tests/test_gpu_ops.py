@@ -5,7 +5,9 @@ the C ABI, is compared with the oracle on the same inputs: bit-exact for element
 broadcast and transposes (fp32 and 16-bit), and within the reference's tolerances otherwise
 (activation 1e-5, reduce 1e-4, layer_norm / rms_norm_rope 1e-4 in fp32).  The BASELINE
 configurations run at full size with their stated tolerances (layer_norm max-abs 1e-2,
-rms_norm_rope max-abs 2e-2, elementwise_add bit-exact)."""
+rms_norm_rope max-abs 2e-2, elementwise_add bit-exact); for 16-bit outputs an element also passes
+when it is within half an output ulp (relative) of the fp32 golden, because above |y| = 2.56
+(bf16) a single correct rounding of the output already exceeds 1e-2."""
 from __future__ import annotations
 
 import numpy as np
@@ -18,6 +20,8 @@ from gpu_util import bits, dev, host, quantize
 pytestmark = pytest.mark.gpu
 
 KINDS = ["f32", "bf16", "f16"]
+# Half a unit in the last place, relative, of a correctly rounded 16-bit output.
+OUT_HALF_ULP = {"bf16": 2.0 ** -8, "f16": 2.0 ** -11}
 
 
 # --------------------------------------------------------------------------- elementwise_add
@@ -192,8 +196,9 @@ def test_layer_norm_config(cuda, hc_lib, oracle, kind):
     b = oracle.uniform(dim, 2, -0.1, 0.1)
     y = hc_lib.layer_norm(dev(x, kind, oracle), dev(g, "f32", oracle), dev(b, "f32", oracle), 1e-5)
     ref = oracle.layer_norm(quantize(x, kind, oracle), g, b, 1e-5)
-    r = assert_close(ref, host(y, oracle), 1e-2, 0.0, "layer_norm config")
-    assert r.max_abs <= 1e-2
+    # max-abs 1e-2, or (where |y| is so large that one 16-bit rounding alone exceeds 1e-2) half an
+    # output ulp relative: CompareArrays semantics, an element fails only if both are exceeded.
+    assert_close(ref, host(y, oracle), 1e-2, OUT_HALF_ULP[kind], "layer_norm config")
 
 
 # --------------------------------------------------------------------------- rms_norm_rope_fused
@@ -219,7 +224,7 @@ def test_rms_norm_rope_heads_and_styles(cuda, hc_lib, oracle, style, H, rot):
         out = hc_lib.rms_norm_rope_fused(dev(x, kind, oracle), dev(w, "f32", oracle), dev(cos, "f32", oracle),
                                          dev(sin, "f32", oracle), rot, 1e-6, heads=Hh, rope_style=style)
         ref = oracle.rms_norm_rope(quantize(x, kind, oracle), w, cos, sin, rot, 1e-6, heads=Hh, style=style)
-        assert_close(ref, host(out, oracle), tol, 1e-4 if kind == "f32" else 0.0, f"{kind} style{style}")
+        assert_close(ref, host(out, oracle), tol, 1e-4 if kind == "f32" else OUT_HALF_ULP[kind], f"{kind} style{style}")
 
 
 def test_rms_norm_rope_config(cuda, hc_lib, oracle):
@@ -235,5 +240,4 @@ def test_rms_norm_rope_config(cuda, hc_lib, oracle):
     del out
     for b in range(B):  # oracle per batch keeps host memory bounded
         ref = oracle.rms_norm_rope(quantize(x[b:b + 1], "bf16", oracle), w, cos, sin, D, 1e-6, heads=Hh, style=1)
-        r = assert_close(ref, got[b:b + 1], 2e-2, 0.0, f"rms_norm_rope config batch {b}")
-        assert r.max_abs <= 2e-2
+        assert_close(ref, got[b:b + 1], 2e-2, OUT_HALF_ULP["bf16"], f"rms_norm_rope config batch {b}")
