@@ -40,9 +40,15 @@ using namespace sm100;
 
 enum class NormKind { kLayerNorm, kRmsRope };
 
-constexpr uint32_t kConsumerWarps = 8;
+// Consumers: kGroups groups of kGroupWarps warps; group g takes this CTA's tiles i = g, g+kGroups,
+// ..., so two tiles are being normalised while further stages are in flight.
+// The number of groups actually used (a.groups <= kGroups) is chosen at launch so that every
+// active group has a tile to work on and at least one more stage is being filled.
+constexpr uint32_t kGroupWarps = 4;
+constexpr uint32_t kGroups = 6;
+constexpr uint32_t kConsumerWarps = kGroupWarps * kGroups;
 constexpr uint32_t kThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
-constexpr uint32_t kMaxStages = 8;
+constexpr uint32_t kMaxStages = 12;
 constexpr uint32_t kSmemBudget = 200 * 1024;
 
 __device__ uint32_t g_norm_error_word;
@@ -67,6 +73,12 @@ struct NormArgs {
     uint32_t param_floats;     // floats of parameters staged in shared memory
     uint32_t param_stride;     // floats per staged parameter vector (lane-transposed, padded)
     uint32_t vec_rope;         // 1: rotary packs never straddle the rotary boundary or the halves
+    float inv_h;               // 1/H
+    uint32_t groups;           // consumer groups in use (<= kGroups)
+    uint32_t xor_partner;      // 1: one pack per lane, rotate-half partner on lane gl ^ G/2
+    FastDiv div_heads, div_S;  // row -> sequence position (row / heads) % S
+
+    __device__ __forceinline__ uint32_t pos_of_row(uint32_t row) const { return div_S.mod(div_heads.div(row)); }
 };
 
 struct RingBars {
@@ -80,10 +92,14 @@ __device__ __forceinline__ float group_sum(float v) {
     return v;
 }
 
+// Reads one 16-byte pack from shared memory with a single 128-bit load (a member-wise copy of the
+// 16-bit struct would become eight 2-byte loads, 4-way bank-conflicted across the warp).
 template <typename T>
 __device__ __forceinline__ void unpack_f(const pack<T>& p, float* f) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(&p);
+    const pack<T>& q = *reinterpret_cast<const pack<T>*>(&raw);
 #pragma unroll
-    for (int e = 0; e < elem<T>::kPack; ++e) f[e] = elem<T>::to_f(p.v[e]);
+    for (int e = 0; e < elem<T>::kPack; ++e) f[e] = elem<T>::to_f(q.v[e]);
 }
 
 // Shared-memory layout of a staged parameter vector, transposed by lane: lane gl of a row group
@@ -137,7 +153,7 @@ __device__ __forceinline__ void process_row(const NormArgs& a, const pack<T>* sr
         float f[P];
         unpack_f<T>(srow[k], f);
 #pragma unroll
-        for (int e = 0; e < P; ++e) s = (KIND == NormKind::kLayerNorm) ? __fadd_rn(s, f[e]) : __fadd_rn(s, __fmul_rn(f[e], f[e]));
+        for (int e = 0; e < P; ++e) s = (KIND == NormKind::kLayerNorm) ? __fadd_rn(s, f[e]) : fmaf(f[e], f[e], s);
     }
     s = group_sum<G>(s);
     float mul, sub = 0.f;
@@ -157,19 +173,47 @@ __device__ __forceinline__ void process_row(const NormArgs& a, const pack<T>* sr
         mul = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(q, static_cast<float>(a.H)), a.eps)));  // inv_std
         sub = mean;
     } else {
-        mul = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, static_cast<float>(a.H)), a.eps)));  // 1/rms
+        // 1/rms with the hardware reciprocal square root: rows are short (128 elements in the
+        // RoPE configuration), so IEEE division and square root per row would cost as many
+        // instructions as the row itself.  Error <= 2 ulp, far inside the tolerances.
+        mul = rsqrtf(fmaf(s, a.inv_h, a.eps));
     }
     // ---- last pass: normalise (+ RoPE) and store ----
-    if (!valid) return;
-    T* yrow = static_cast<T*>(a.y) + row * a.H;
     const uint32_t half = a.rot / 2;
     const float* cs = nullptr;
     const float* sn = nullptr;
     if (KIND == NormKind::kRmsRope) {
-        const uint32_t s_pos = static_cast<uint32_t>((row / a.heads) % a.S);
+        const uint32_t s_pos = valid ? a.pos_of_row(static_cast<uint32_t>(row)) : 0u;
         cs = a.cos_t + static_cast<size_t>(s_pos) * half;
         sn = a.sin_t + static_cast<size_t>(s_pos) * half;
+        if (a.xor_partner) {
+            // One pack per lane and rotate-half over the whole row: the partner of lane gl's pack
+            // is lane gl ^ G/2's pack, so the normalised partner values come over a shuffle
+            // (every lane of the warp executes this branch: the flag is kernel-wide).
+            float f[P], g[P], c[P], z[P], out[P];
+            unpack_f<T>(srow[gl], f);
+            load_params<P, G>(params, gl, g);
+            const bool first = gl < G / 2;
+            const uint32_t i0 = (first ? gl : gl - G / 2) * P;
+            ldg_f32<P>(cs + i0, c);
+            ldg_f32<P>(sn + i0, z);
+#pragma unroll
+            for (int e = 0; e < P; ++e) out[e] = f[e] * mul * g[e];
+            const float zs = first ? -1.f : 1.f;  // first half: y c - p z; second: p z + y c
+#pragma unroll
+            for (int e = 0; e < P; ++e) {
+                const float partner = __shfl_xor_sync(0xffffffffu, out[e], G / 2);
+                out[e] = fmaf(out[e], c[e], zs * partner * z[e]);
+            }
+            if (valid) {
+                T* yrow = static_cast<T*>(a.y) + row * a.H;
+                st_stream(reinterpret_cast<pack<T>*>(yrow) + gl, pack_from_f<T>(out));
+            }
+            return;
+        }
     }
+    if (!valid) return;
+    T* yrow = static_cast<T*>(a.y) + row * a.H;
     for (uint32_t k = gl; k < packs; k += G) {
         const uint32_t d0 = k * P;
         float f[P], g[P];
@@ -180,10 +224,7 @@ __device__ __forceinline__ void process_row(const NormArgs& a, const pack<T>* sr
             float b[P];
             load_params<P, G>(params + a.param_stride, k, b);
 #pragma unroll
-            for (int e = 0; e < P; ++e) {
-                const float nrm = __fmul_rn(__fsub_rn(f[e], sub), mul);
-                out[e] = __fadd_rn(__fmul_rn(nrm, g[e]), b[e]);
-            }
+            for (int e = 0; e < P; ++e) out[e] = fmaf((f[e] - sub) * mul, g[e], b[e]);
         } else {
 #pragma unroll
             for (int e = 0; e < P; ++e) out[e] = __fmul_rn(__fmul_rn(f[e], mul), g[e]);
@@ -196,8 +237,8 @@ __device__ __forceinline__ void process_row(const NormArgs& a, const pack<T>* sr
 #pragma unroll
                     for (int e = 0; e < P; e += 2) {
                         const float ye = out[e], yo = out[e + 1];
-                        out[e] = __fsub_rn(__fmul_rn(ye, c[e / 2]), __fmul_rn(yo, z[e / 2]));
-                        out[e + 1] = __fadd_rn(__fmul_rn(ye, z[e / 2]), __fmul_rn(yo, c[e / 2]));
+                        out[e] = fmaf(ye, c[e / 2], -yo * z[e / 2]);
+                        out[e + 1] = fmaf(ye, z[e / 2], yo * c[e / 2]);
                     }
                 } else {
                     const bool first = d0 < half;
@@ -207,11 +248,11 @@ __device__ __forceinline__ void process_row(const NormArgs& a, const pack<T>* sr
                     load_params<P, G>(params, kp, gp);
                     ldg_f32<P>(cs + (first ? d0 : d0 - half), c);
                     ldg_f32<P>(sn + (first ? d0 : d0 - half), z);
+                    const float zs = first ? -1.f : 1.f;  // first half: y c - p z; second: p z + y c
 #pragma unroll
                     for (int e = 0; e < P; ++e) {
-                        const float partner = __fmul_rn(__fmul_rn(fp[e], mul), gp[e]);
-                        out[e] = first ? __fsub_rn(__fmul_rn(out[e], c[e]), __fmul_rn(partner, z[e]))
-                                       : __fadd_rn(__fmul_rn(partner, z[e]), __fmul_rn(out[e], c[e]));
+                        const float partner = fp[e] * mul * gp[e];
+                        out[e] = fmaf(out[e], c[e], zs * partner * z[e]);
                     }
                 }
             } else if (d0 < a.rot) {
@@ -247,10 +288,7 @@ __device__ __forceinline__ void process_row(const NormArgs& a, const pack<T>* sr
                 }
             }
         }
-        pack<T> o;
-#pragma unroll
-        for (int e = 0; e < P; ++e) o.v[e] = elem<T>::from_f(out[e]);
-        st_stream(reinterpret_cast<pack<T>*>(yrow) + k, o);
+        st_stream(reinterpret_cast<pack<T>*>(yrow) + k, pack_from_f<T>(out));
     }
 }
 
@@ -269,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1) rowstream_kernel(NormArgs a) {
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < a.stages; ++s) {
             mbar_init(&bars->full[s], 1);
-            mbar_init(&bars->empty[s], kConsumerWarps);
+            mbar_init(&bars->empty[s], kGroupWarps);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -323,14 +361,18 @@ __global__ void __launch_bounds__(kThreads, 1) rowstream_kernel(NormArgs a) {
         // ================================ consumers ================================
         constexpr uint32_t kRowsPerPass = 32 / G;
         const uint32_t sub = lane / G, gl = lane % G;
-        uint32_t stage = 0, phase = 0;
-        for (uint64_t t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        const uint32_t grp = warp / kGroupWarps, gw = warp % kGroupWarps;
+        for (uint64_t i = grp; grp < a.groups; i += a.groups) {
+            const uint64_t t = blockIdx.x + i * gridDim.x;
+            if (t >= num_tiles) break;
+            const uint32_t stage = static_cast<uint32_t>(i % a.stages);
+            const uint32_t phase = static_cast<uint32_t>((i / a.stages) & 1);
             bool ok = mbar_wait_bounded(&bars->full[stage], phase, abort_flag, &g_norm_error_word, 2u);
             if (!__all_sync(0xffffffffu, ok)) break;
             const uint64_t r0 = t * a.tile_rows;
             const uint32_t nr = static_cast<uint32_t>((a.rows - r0 < a.tile_rows) ? (a.rows - r0) : a.tile_rows);
             const uint8_t* tile = ring + stage * a.tile_bytes;
-            for (uint32_t rb = warp * kRowsPerPass; rb < nr; rb += kConsumerWarps * kRowsPerPass) {
+            for (uint32_t rb = gw * kRowsPerPass; rb < nr; rb += kGroupWarps * kRowsPerPass) {
                 const uint32_t rr = rb + sub;
                 const bool valid = rr < nr;
                 process_row<T, KIND, G>(a, reinterpret_cast<const pack<T>*>(tile + (valid ? rr : rb) * row_bytes),
@@ -338,10 +380,6 @@ __global__ void __launch_bounds__(kThreads, 1) rowstream_kernel(NormArgs a) {
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->empty[stage]);
-            if (++stage == a.stages) {
-                stage = 0;
-                phase ^= 1;
-            }
         }
     }
     __syncthreads();
@@ -440,12 +478,15 @@ int launch_rowstream(NormArgs a, cudaStream_t s) {
     if (a.param_floats * 4ull > 64 * 1024) return fail(HC_ERR_UNSUPPORTED, "row of %u elements too long", a.H);
     a.vec_rope = (KIND == NormKind::kRmsRope) && a.rot % P == 0 && (a.rot / 2) % P == 0 &&
                  (a.rot / 2) % 4 == 0 && aligned16(a.cos_t) && aligned16(a.sin_t);
+    a.xor_partner = a.vec_rope && a.style == 1 && a.rot == a.H && packs == G;
+    a.div_heads.init(a.heads);
+    a.div_S.init(a.S);
     const uint32_t row_bytes = a.H * static_cast<uint32_t>(sizeof(T));
-    const uint32_t rows_per_pass = kConsumerWarps * (32 / G);
+    const uint32_t rows_per_pass = kGroupWarps * (32 / G);  // rows one consumer group takes at once
     const uint32_t param_bytes = ((a.param_floats * 4 + 127) & ~127u);
-    // Tile: whole passes of the consumer warps, 16..64 KB when rows allow.
+    // Tile: whole passes of a consumer group, up to 16 KB when rows allow.
     uint32_t passes = 1;
-    while (passes < 64 && rows_per_pass * (passes * 2) * row_bytes <= 32 * 1024) passes *= 2;
+    while (passes < 64 && rows_per_pass * (passes * 2) * row_bytes <= 16 * 1024) passes *= 2;
     a.tile_rows = rows_per_pass * passes;
     if (static_cast<uint64_t>(a.tile_rows) * row_bytes > 64 * 1024) {
         a.tile_rows = (64 * 1024) / row_bytes;
@@ -463,6 +504,7 @@ int launch_rowstream(NormArgs a, cudaStream_t s) {
         if (a.stages > kMaxStages) a.stages = kMaxStages;
         if (a.stages < 2) return fail(HC_ERR_UNSUPPORTED, "row of %u bytes too long for the row-stream kernel", row_bytes);
     }
+    a.groups = a.stages - 1 < kGroups ? a.stages - 1 : kGroups;  // keep one stage filling
     const size_t smem = 128 + param_bytes + static_cast<size_t>(a.stages) * a.tile_bytes + bar_bytes;
     static bool attr_set = false;
     if (!attr_set) {
@@ -549,5 +591,6 @@ extern "C" int hc_rms_norm_rope_fused_launch(const void* x, const float* weight,
     a.x = x; a.y = out; a.gamma = weight; a.beta = nullptr; a.cos_t = cos_table; a.sin_t = sin_table;
     a.rows = static_cast<uint32_t>(rows); a.H = t->H; a.eps = t->eps;
     a.heads = heads; a.S = t->S; a.rot = t->rotaryDim; a.style = rope_style;
+    a.inv_h = 1.0f / static_cast<float>(t->H);
     return dispatch_rownorm<NormKind::kRmsRope>(dtype, a, stream, "rms_norm_rope_fused");
 }
