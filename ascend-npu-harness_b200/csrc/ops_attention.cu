@@ -74,7 +74,7 @@ __device__ uint32_t g_fa_error_word;
 struct Params {
     void* o;
     float* lse;
-    uint32_t S_q, S_k, BH, n_qblk, num_units;
+    uint32_t S_q, S_k, BH, n_qblk, num_pairs;  // num_pairs = BH * ceil(n_qblk / 2)
     float scale_log2;  // softmax scale * log2(e), > 0
     uint32_t causal;
 };
@@ -86,12 +86,35 @@ struct Bars {
     uint64_t mma_done;
 };
 
-__device__ __forceinline__ void unit_coords(const Params& p, uint32_t u, uint32_t& bh, uint32_t& qb) {
-    uint32_t r = u / p.BH;
-    bh = u - r * p.BH;
-    // Causal: hand out the longest query blocks first so the persistent CTAs finish together.
-    qb = p.causal ? (p.n_qblk - 1 - r) : r;
-}
+// The work units (head, 256-row query block) of this CTA.  Units are handed out as pairs
+// (qb, n_qblk-1-qb) of the same head: under the causal mask the two blocks of a pair need
+// n_qblk+1 key tiles together whatever qb is, so a static round-robin over pairs gives every CTA
+// the same work (to within one pair) without a scheduler in global memory.  Pairs are numbered
+// head-major, so the CTAs in flight work on a few consecutive heads whose K/V tiles are fetched
+// from HBM once and then served from L2.  The longer block of a pair comes first.
+struct UnitSeq {
+    uint32_t pi = blockIdx.x;
+    uint32_t second = 0;
+    __device__ __forceinline__ bool next(const Params& p, uint32_t& bh, uint32_t& qb) {
+        const uint32_t per_head = (p.n_qblk + 1) / 2;
+        while (pi < p.num_pairs) {
+            bh = pi / per_head;
+            const uint32_t j = pi - bh * per_head;
+            if (!second) {
+                second = 1;
+                qb = p.n_qblk - 1 - j;
+                return true;
+            }
+            second = 0;
+            pi += gridDim.x;
+            if (j != p.n_qblk - 1 - j) {  // the middle block of an odd count has no partner
+                qb = j;
+                return true;
+            }
+        }
+        return false;
+    }
+};
 
 __device__ __forceinline__ uint32_t kv_tiles_for(const Params& p, uint32_t row0) {
     uint32_t nk = (p.S_k + kBN - 1) / kBN;
@@ -174,10 +197,11 @@ __device__ __forceinline__ void reg_dealloc() {
 // Pairs (c, c+1) of a 128-key row computed with the FMA-pipe exponential: pair index % 8 below
 // HC_FA_POLY_PER8 (the rest go to MUFU ex2).  With MUFU alone the two softmax warpgroups would
 // need as many MUFU cycles per KV tile as the tensor core needs for the four MMAs.
-#ifndef HC_FA_POLY_PER8
-#define HC_FA_POLY_PER8 0
+#ifndef HC_FA_POLY_MASK
+#define HC_FA_POLY_MASK 0x00
 #endif
-__device__ __forceinline__ constexpr bool poly_pair(int pair) { return (pair & 7) < HC_FA_POLY_PER8; }
+// bit (pair % 8) of HC_FA_POLY_MASK set -> that pair uses the FMA-pipe exponential
+__device__ __forceinline__ constexpr bool poly_pair(int pair) { return (HC_FA_POLY_MASK >> (pair & 7)) & 1; }
 
 template <bool kBF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
@@ -263,9 +287,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t pend_valid = 0, pend_phase = 0;
             int32_t q_pending = -1;
             bool ok = true;
-            for (uint32_t u = blockIdx.x; u < p.num_units && ok; u += gridDim.x, ++q_iter) {
-                uint32_t bh, qb;
-                unit_coords(p, u, bh, qb);
+            UnitSeq seq;
+            uint32_t bh, qb;
+            for (; ok && seq.next(p, bh, qb); ++q_iter) {
                 const uint32_t row0 = qb * 2 * kBM;
                 const uint32_t nkv = kv_tiles_for(p, row0 + kBM);
                 if (!mbar_wait_bounded(&bars->q_empty, (q_iter & 1) ^ 1, abort_flag, &g_fa_error_word, kErrProducerQ)) {
@@ -341,9 +365,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 return true;
             };
-            for (uint32_t u = blockIdx.x; u < p.num_units && ok; u += gridDim.x, ++q_iter) {
-                uint32_t bh, qb;
-                unit_coords(p, u, bh, qb);
+            UnitSeq seq;
+            uint32_t bh, qb;
+            for (; ok && seq.next(p, bh, qb); ++q_iter) {
                 const uint32_t row0 = qb * 2 * kBM;
                 const uint32_t n0 = kv_tiles_for(p, row0);
                 const uint32_t nkv = kv_tiles_for(p, row0 + kBM);
@@ -406,9 +430,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tS = tmem_base + wg * 128 + lane_field;
         const uint32_t tO = tmem_base + 256 + wg * 128 + lane_field;
         uint32_t s_par = 0, o_par = 0;
-        for (uint32_t u = blockIdx.x; u < p.num_units; u += gridDim.x) {
-            uint32_t bh, qb;
-            unit_coords(p, u, bh, qb);
+        UnitSeq seq;
+        uint32_t bh, qb;
+        while (seq.next(p, bh, qb)) {
             const uint32_t row0 = qb * 2 * kBM + wg * kBM;
             const uint32_t row = row0 + r_local;
             const uint32_t n_i = kv_tiles_for(p, row0);
@@ -671,9 +695,9 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
     prm.S_k = t->S_k;
     prm.BH = static_cast<uint32_t>(BH);
     prm.n_qblk = (t->S_q + 2 * kBM - 1) / (2 * kBM);
-    uint64_t units = BH * prm.n_qblk;
-    if (units > 0xffffffffull) return fail(HC_ERR_UNSUPPORTED, "flash_attention: too many work units");
-    prm.num_units = static_cast<uint32_t>(units);
+    const uint64_t pairs = BH * ((prm.n_qblk + 1) / 2);
+    if (BH * prm.n_qblk > 0xffffffffull) return fail(HC_ERR_UNSUPPORTED, "flash_attention: too many work units");
+    prm.num_pairs = static_cast<uint32_t>(pairs);
     prm.scale_log2 = t->scale * 1.4426950408889634f;
     prm.causal = t->maskType;
     static bool attr_set[2] = {false, false};
@@ -684,7 +708,7 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
         attr_set[kBF16] = true;
     }
     uint32_t grid = static_cast<uint32_t>(sm_count());
-    if (grid > prm.num_units) grid = prm.num_units;
+    if (grid > prm.num_pairs) grid = prm.num_pairs;
     fa_fwd_tc_kernel<kBF16><<<grid, kThreads, kSmemBytes, stream>>>(tmq, tmk, tmv, prm);
     t_last_path = 1;
     return check_launch("fa_fwd_tc_kernel");
