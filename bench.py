@@ -59,8 +59,21 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def profile_traffic(name: str):
-    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name>.md ("traffic_bytes_per_launch: N")."""
+# op -> the profiles/<file>.md that records its ncu capture (named for the kernel and workload)
+PROFILE_FILES = {
+    "flash_attention_fwd_causal": "flash_attention_fwd_causal_B16H32S8192D128",
+    "matmul_bias": "matmul_bias_8192x8192x8192",
+    "layer_norm": "layer_norm_16384x4096_bf16",
+    "rms_norm_rope_fused": "rms_norm_rope_fused_8x4096x32x128_bf16",
+    "elementwise_add": "elementwise_add_4096x8192_f16",
+}
+
+
+def profile_traffic(op: str):
+    """Per-launch DRAM bytes recorded from an ncu capture ("traffic_bytes_per_launch: N" in its profile)."""
+    name = PROFILE_FILES.get(op)
+    if name is None:
+        return None
     p = ROOT / "profiles" / f"{name}.md"
     if not p.exists():
         return None
@@ -325,7 +338,7 @@ def run_ours(args):
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops"],
                 "peak_source": f"{peak_src} bf16_tflops (burst: the kernel is timed alone)",
-                "traffic": profile_traffic("flash_attention_fwd_causal_B16H32S8192D128"),
+                "traffic": profile_traffic("flash_attention_fwd_causal"),
                 "algorithmic_flops_per_launch": flops_rank}
     del o
 
@@ -432,7 +445,9 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
         out["matmul_bias"] = {"value": d.world * tf, "unit": "TFLOP/s", "per_gpu": tf, "ms": ms,
                               "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"],
                                            "unit": "TFLOP/s", "frac": tf / peaks["bf16_tflops"],
-                                           "algorithmic_flops_per_launch": fl}}
+                                           "algorithmic_flops_per_launch": fl,
+                                           "algorithmic_bytes_per_launch": 3 * M * N * 2 + N * 2,
+                                           "traffic": profile_traffic("matmul_bias")}}
         del A, B, bias, C
 
     if "layer_norm" in want:  # [16384, 4096] bf16, fp32 gamma/beta
