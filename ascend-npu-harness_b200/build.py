@@ -1,4 +1,8 @@
-"""Builds the B200 operator library (lib/libhc_b200.so) from csrc/*.cu with nvcc for sm_100a.
+"""Builds the B200 operator library and its C++ host layer.
+
+  lib/libhc_b200.so    : csrc/*.cu compiled with nvcc for sm_100a -- the C-ABI (include/*.h)
+  lib/libhc_harness.so : host/src/*.cpp compiled with g++ -- the harness::device runtime and the
+                         per-op C++ runners (host/include/harness/*.hpp), linked to libhc_b200.so
 
 Usage: python build.py [--force] [--verbose]
 
@@ -22,6 +26,9 @@ CSRC = HERE / "csrc"
 LIB = HERE / "lib"
 INCLUDE = ROOT / "include"
 TARGET = LIB / "libhc_b200.so"
+HOST = HERE / "host"
+HOST_TARGET = LIB / "libhc_harness.so"
+HOST_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-Wall", "-Wextra", f"-I{INCLUDE}", f"-I{HOST / 'include'}"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
@@ -77,7 +84,25 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr[-6000:]}")
+    build_host(force, verbose)
     return TARGET
+
+
+def build_host(force: bool = False, verbose: bool = False) -> Path:
+    """Compiles the C++ host layer (host/src/*.cpp) into lib/libhc_harness.so, linked to libhc_b200.so."""
+    srcs = sorted((HOST / "src").glob("*.cpp"))
+    deps = srcs + sorted((HOST / "include").rglob("*.hpp")) + sorted(INCLUDE.glob("*.h")) + [TARGET]
+    if not force and not _stale(HOST_TARGET, deps):
+        return HOST_TARGET
+    cxx = shutil.which("g++") or "g++"
+    cmd = [cxx, *HOST_FLAGS, "-shared", *map(str, srcs), "-o", str(HOST_TARGET), f"-L{LIB}", "-lhc_b200",
+           "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"host layer build failed:\n{r.stderr[-6000:]}")
+    return HOST_TARGET
 
 
 if __name__ == "__main__":

@@ -168,6 +168,12 @@ int hc_get_device(int* device) {
     return ok();
 }
 
+int hc_driver_version(int* version) {
+    if (!version) return fail(HC_ERR_INVALID, "hc_driver_version: null");
+    HC_CHECK_CUDA(cudaDriverGetVersion(version));
+    return ok();
+}
+
 int hc_device_sm_count(int* sms) {
     if (!sms) return fail(HC_ERR_INVALID, "hc_device_sm_count: null");
     int dev = 0;

@@ -194,9 +194,11 @@ __device__ __forceinline__ void reg_dealloc() {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
-// Pairs (c, c+1) of a 128-key row computed with the FMA-pipe exponential: pair index % 8 below
-// HC_FA_POLY_PER8 (the rest go to MUFU ex2).  With MUFU alone the two softmax warpgroups would
-// need as many MUFU cycles per KV tile as the tensor core needs for the four MMAs.
+// Pairs (c, c+1) of a 128-key row may be computed with the FMA-pipe exponential instead of MUFU
+// ex2, selected by bit (pair % 8) of HC_FA_POLY_MASK.  With MUFU alone the two softmax
+// warpgroups need about as many MUFU cycles per KV tile as the tensor core needs for the four
+// MMAs; on B200 every tried mask was slower than MUFU alone (the extra FMA/ALU instructions cost
+// more issue slots than the MUFU wait they hide), so the default mask is empty.
 #ifndef HC_FA_POLY_MASK
 #define HC_FA_POLY_MASK 0x00
 #endif

@@ -1,28 +1,33 @@
 // layer_norm and rms_norm_rope_fused: row-wise normalisations, HBM-bound.
 //
-// Row-stream design (one persistent CTA per SM):
+// Row-stream design (one persistent CTA per SM, 800 threads):
 //   * a producer thread copies tiles of whole consecutive rows from HBM into a ring of
 //     shared-memory stages with single bulk TMA copies (cp.async.bulk, completion on an mbarrier),
 //     keeping up to ~190 KB per SM in flight -- enough to cover HBM latency at full bandwidth
 //     without holding rows in registers;
-//   * eight consumer warps take the rows of the current stage (a group of G = 8/16/32 lanes per
-//     row), reduce the row from shared memory with shuffles, then make one more pass over the
-//     row in shared memory to normalise, apply the per-column parameters (staged in shared memory
-//     once per CTA) and, for RoPE, read the rotation partner of each element straight from the
-//     staged row; outputs leave as 16-byte streaming stores;
+//   * up to six consumer groups of four warps take turns on the stages (group g takes this CTA's
+//     tiles g, g+groups, ...); inside a tile a group of G = 8/16/32 lanes owns one row, reduces it
+//     from shared memory with shuffles, then makes one more pass over the row in shared memory to
+//     normalise, apply the per-column parameters (staged in shared memory once per CTA, in a
+//     lane-transposed order so every lane reads them as conflict-free 16-byte words) and, for
+//     RoPE, take the rotation partner of each element from the staged row or from the partner
+//     lane by shuffle; outputs leave as 16-byte streaming stores;
 //   * each consumer warp releases the stage through an mbarrier when its rows are done.
 // HBM therefore sees exactly one read and one write per element.
 //
-// Arithmetic mirrors the reference goldens step by step with explicitly rounded fp32 ops:
+// Arithmetic follows the reference goldens step by step:
 //   layer_norm          ops/layer_norm/golden/layer_norm_golden.cpp:15-39 (two-pass mean/var,
-//                       inv_std = 1/sqrt(var+eps), y = (x-mean)*inv_std*gamma + beta)
+//                       inv_std = 1/sqrt(var+eps), y = (x-mean)*inv_std*gamma + beta); the
+//                       statistics use correctly rounded fp32 adds, division and square root;
 //   rms_norm_rope_fused ops/rms_norm_rope_fused/golden/rms_norm_rope_fused_golden.cpp:20-51
-//                       (rms = sqrt(mean(x^2)+eps), y = x/rms*w, then the rotation)
+//                       (rms = sqrt(mean(x^2)+eps), y = x/rms*w, then the rotation).
 // Differences from the goldens: sums are fp32 (per-lane sequential, then a shuffle tree) instead
-// of sequential fp64, and x/rms is computed as x*(1/rms) (one extra rounding, <= 1 ulp): an IEEE
-// division per element would make the kernel instruction-bound instead of HBM-bound.
+// of sequential fp64; x/rms is computed as x*(1/rms); the per-element products may be fused into
+// multiply-adds and RMS uses rsqrtf (a few ulp of fp32, far below the 16-bit output rounding):
+// an IEEE division per element would make the kernel instruction-bound instead of HBM-bound.
+// The scalar fallback kernel keeps every fp32 operation explicitly rounded.
 //
-// Rows that are not a multiple of 16 bytes, or unaligned buffers, use a simple scalar kernel.
+// Rows that are not a multiple of 16 bytes, or unaligned buffers, use that simple scalar kernel.
 // Waits are bounded like the tensor-core kernels'; an expired wait is reported through
 // hc_check_device_error().
 #include <cuda_runtime.h>

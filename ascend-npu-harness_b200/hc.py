@@ -91,6 +91,7 @@ SIGNATURES = {
     "hc_device_count": (_i, [_P(_i)]),
     "hc_set_device": (_i, [_i]),
     "hc_get_device": (_i, [_P(_i)]),
+    "hc_driver_version": (_i, [_P(_i)]),
     "hc_device_sm_count": (_i, [_P(_i)]),
     "hc_device_name": (_i, [C.c_char_p, _sz]),
     "hc_malloc": (_i, [_P(_vp), _sz]),

@@ -61,6 +61,8 @@ int hc_device_count(int* count);
 /* ascend::SetDevice / GetCurrentDevice (ascend_runtime.hpp:21-22). */
 int hc_set_device(int device);
 int hc_get_device(int* device);
+/* ascend::GetDriverVersion (ascend_runtime.hpp:46): CUDA driver version, e.g. 12090. */
+int hc_driver_version(int* version);
 /* Streaming-multiprocessor count and name of the current device. */
 int hc_device_sm_count(int* sms);
 int hc_device_name(char* buf, size_t buflen);
