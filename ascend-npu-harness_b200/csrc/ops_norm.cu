@@ -1,19 +1,25 @@
 // layer_norm and rms_norm_rope_fused: row-wise normalisations, HBM-bound.
 //
-// Row-stream design (one persistent CTA per SM, 800 threads):
+// Two kernel shapes; both read every element from HBM once and write it once.
+//
+// Row-stream kernel (short and medium rows; all RMSNorm+RoPE shapes), one persistent CTA per SM,
+// 800 threads:
 //   * a producer thread copies tiles of whole consecutive rows from HBM into a ring of
 //     shared-memory stages with single bulk TMA copies (cp.async.bulk, completion on an mbarrier),
-//     keeping up to ~190 KB per SM in flight -- enough to cover HBM latency at full bandwidth
-//     without holding rows in registers;
+//     keeping up to ~190 KB per SM in flight without holding rows in registers;
 //   * up to six consumer groups of four warps take turns on the stages (group g takes this CTA's
 //     tiles g, g+groups, ...); inside a tile a group of G = 8/16/32 lanes owns one row, reduces it
-//     from shared memory with shuffles, then makes one more pass over the row in shared memory to
-//     normalise, apply the per-column parameters (staged in shared memory once per CTA, in a
-//     lane-transposed order so every lane reads them as conflict-free 16-byte words) and, for
-//     RoPE, take the rotation partner of each element from the staged row or from the partner
-//     lane by shuffle; outputs leave as 16-byte streaming stores;
-//   * each consumer warp releases the stage through an mbarrier when its rows are done.
-// HBM therefore sees exactly one read and one write per element.
+//     with shuffles, then normalises it from shared memory and leaves with 16-byte streaming
+//     stores; each consumer warp releases the stage through an mbarrier when its rows are done;
+//   * row processing is specialised at compile time where the shape allows: rows of exactly
+//     32*KPL packs (unrolled LayerNorm), and rotate-half RoPE over the whole row, where lane gl
+//     holds pack gl and its rotation partner pack gl+G (no data from other lanes, weights kept in
+//     registers); both do their arithmetic on f32x2 pairs.  A generic loop handles the rest.
+//
+// Direct LayerNorm kernel (rows of 1024*KPL 16-bit / 512*KPL fp32 elements): a 128-thread group
+// owns whole rows, keeps its share of the current row in registers and issues the streaming loads
+// of its next row before working on the current one; one-pass shifted statistics with an exact
+// fallback pass, combined across the group's warps through shared memory and a named barrier.
 //
 // Arithmetic follows the reference goldens step by step:
 //   layer_norm          ops/layer_norm/golden/layer_norm_golden.cpp:15-39 (two-pass mean/var,
@@ -21,11 +27,13 @@
 //                       statistics use correctly rounded fp32 adds, division and square root;
 //   rms_norm_rope_fused ops/rms_norm_rope_fused/golden/rms_norm_rope_fused_golden.cpp:20-51
 //                       (rms = sqrt(mean(x^2)+eps), y = x/rms*w, then the rotation).
-// Differences from the goldens: sums are fp32 (per-lane sequential, then a shuffle tree) instead
-// of sequential fp64; x/rms is computed as x*(1/rms); the per-element products may be fused into
-// multiply-adds and RMS uses rsqrtf (a few ulp of fp32, far below the 16-bit output rounding):
-// an IEEE division per element would make the kernel instruction-bound instead of HBM-bound.
-// The scalar fallback kernel keeps every fp32 operation explicitly rounded.
+// Differences from the goldens: sums are fp32 (per-lane partial sums, then a shuffle tree)
+// instead of sequential fp64 -- for LayerNorm taken over deviations from the row's first element,
+// which keeps the mean accurate for rows near a large constant; x/rms is computed as x*(1/rms);
+// per-element products may be fused into multiply-adds and RMS uses rsqrtf (a few ulp of fp32,
+// far below the 16-bit output rounding): an IEEE division per element would make the kernel
+// instruction-bound instead of HBM-bound.  The scalar fallback kernel keeps every fp32 operation
+// explicitly rounded.
 //
 // Rows that are not a multiple of 16 bytes, or unaligned buffers, use that simple scalar kernel.
 // Waits are bounded like the tensor-core kernels'; an expired wait is reported through
@@ -153,17 +161,19 @@ __device__ __forceinline__ void process_row(const NormArgs& a, const pack<T>* sr
     const float invH = 1.0f / static_cast<float>(a.H);
     (void)invH;
     // ---- pass 1 (and 2 for LayerNorm): statistics from shared memory ----
+    const float K = (KIND == NormKind::kLayerNorm) ? elem<T>::to_f(srow[0].v[0]) : 0.f;  // LayerNorm shift
     float s = 0.f;
     for (uint32_t k = gl; k < packs; k += G) {
         float f[P];
         unpack_f<T>(srow[k], f);
 #pragma unroll
-        for (int e = 0; e < P; ++e) s = (KIND == NormKind::kLayerNorm) ? __fadd_rn(s, f[e]) : fmaf(f[e], f[e], s);
+        for (int e = 0; e < P; ++e)
+            s = (KIND == NormKind::kLayerNorm) ? __fadd_rn(s, __fsub_rn(f[e], K)) : fmaf(f[e], f[e], s);
     }
     s = group_sum<G>(s);
     float mul, sub = 0.f;
     if (KIND == NormKind::kLayerNorm) {
-        const float mean = __fdiv_rn(s, static_cast<float>(a.H));
+        const float mean = __fadd_rn(K, __fdiv_rn(s, static_cast<float>(a.H)));
         float q = 0.f;
         for (uint32_t k = gl; k < packs; k += G) {
             float f[P];
@@ -297,7 +307,196 @@ __device__ __forceinline__ void process_row(const NormArgs& a, const pack<T>* sr
     }
 }
 
-template <typename T, NormKind KIND, int G>
+// ---- 16-byte packs as float2 pairs (element 2i in .x, 2i+1 in .y) ----
+template <typename T>
+struct Pk;
+template <>
+struct Pk<bf16_t> {
+    static constexpr int N2 = 4;
+    __device__ static void unpack(const uint4& r, float2* f) {
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f[i] = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+    }
+    __device__ static uint4 pack(const float2* f) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __nv_bfloat162 h = __float22bfloat162_rn(f[i]);
+            w[i] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
+};
+template <>
+struct Pk<f16_t> {
+    static constexpr int N2 = 4;
+    __device__ static void unpack(const uint4& r, float2* f) {
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f[i] = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    }
+    __device__ static uint4 pack(const float2* f) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            __half2 h = __float22half2_rn(f[i]);
+            w[i] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        return make_uint4(w[0], w[1], w[2], w[3]);
+    }
+};
+template <>
+struct Pk<float> {
+    static constexpr int N2 = 2;
+    __device__ static void unpack(const uint4& r, float2* f) {
+        f[0] = make_float2(__uint_as_float(r.x), __uint_as_float(r.y));
+        f[1] = make_float2(__uint_as_float(r.z), __uint_as_float(r.w));
+    }
+    __device__ static uint4 pack(const float2* f) {
+        return make_uint4(__float_as_uint(f[0].x), __float_as_uint(f[0].y), __float_as_uint(f[1].x),
+                          __float_as_uint(f[1].y));
+    }
+};
+
+// Shift for the LayerNorm mean: the row's first element.  The mean is computed as
+// K + sum(x - K) / H, so the fp32 partial sums hold deviations from a value of the row instead of
+// the raw values: the error of the mean then stays a small fraction of the row's spread even when
+// |mean| >> spread (rows near a large constant), where a plain fp32 sum of x would lose the mean.
+// (The reference golden sums in fp64, layer_norm_golden.cpp:19-23.)
+template <typename T>
+__device__ __forceinline__ float row_shift(const T* row) {
+    return elem<T>::to_f(row[0]);
+}
+
+// Row processors specialised at compile time for rows of exactly G * KPL packs: lane gl of the
+// row group owns packs gl + G*j, every loop is unrolled and the arithmetic runs on f32x2 pairs
+// (one FFMA2/FADD2/FMUL2 per two elements).  The generic process_row above handles every
+// other shape.
+
+// LayerNorm: mean, centred sum of squares, normalise -- three passes over the staged row.  The
+// pass loops are unrolled only 4 / 2 deep: at 800 threads a thread has 80 registers, and fully
+// unrolled passes would hoist every load of the row and spill.
+template <typename T, int G, int KPL>
+__device__ __forceinline__ void ln_row_fast(const NormArgs& a, const uint4* srow, const float* params, uint64_t row,
+                                            uint32_t gl, bool valid) {
+    constexpr int N2 = Pk<T>::N2, P = 2 * N2;
+    // Sum of deviations from the row's first element (see row_shift).
+    const float K = row_shift(reinterpret_cast<const T*>(srow));
+    const float2 nk = make_float2(-K, -K);
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = acc0;
+#pragma unroll(KPL > 4 ? 4 : 2)
+    for (int j = 0; j < KPL; ++j) {
+        float2 f[N2];
+        Pk<T>::unpack(srow[gl + G * j], f);
+#pragma unroll
+        for (int i = 0; i < N2; ++i) {
+            if (i & 1) acc1 = __fadd2_rn(acc1, __fadd2_rn(f[i], nk));
+            else acc0 = __fadd2_rn(acc0, __fadd2_rn(f[i], nk));
+        }
+    }
+    const float mean =
+        __fadd_rn(K, __fdiv_rn(group_sum<G>((acc0.x + acc0.y) + (acc1.x + acc1.y)), static_cast<float>(a.H)));
+    const float2 nmean = make_float2(-mean, -mean);
+    acc0 = acc1 = make_float2(0.f, 0.f);
+#pragma unroll(KPL > 4 ? 4 : 2)
+    for (int j = 0; j < KPL; ++j) {
+        float2 f[N2];
+        Pk<T>::unpack(srow[gl + G * j], f);
+#pragma unroll
+        for (int i = 0; i < N2; ++i) {
+            const float2 d = __fadd2_rn(f[i], nmean);
+            if (i & 1) acc1 = __ffma2_rn(d, d, acc1);
+            else acc0 = __ffma2_rn(d, d, acc0);
+        }
+    }
+    const float q = group_sum<G>((acc0.x + acc0.y) + (acc1.x + acc1.y));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(q, static_cast<float>(a.H)), a.eps)));
+    if (!valid) return;
+    const float2 inv2 = make_float2(inv, inv);
+    uint4* yrow = reinterpret_cast<uint4*>(static_cast<T*>(a.y) + row * a.H);
+#pragma unroll 2
+    for (int j = 0; j < KPL; ++j) {
+        const uint32_t k = gl + G * j;
+        float2 f[N2], o[N2];
+        float g[P], b[P];
+        Pk<T>::unpack(srow[k], f);
+        load_params<P, G>(params, k, g);
+        load_params<P, G>(params + a.param_stride, k, b);
+#pragma unroll
+        for (int i = 0; i < N2; ++i) {
+            const float2 y = __fmul2_rn(__fadd2_rn(f[i], nmean), inv2);
+            o[i] = __ffma2_rn(y, make_float2(g[2 * i], g[2 * i + 1]), make_float2(b[2 * i], b[2 * i + 1]));
+        }
+        __stcs(yrow + k, Pk<T>::pack(o));
+    }
+}
+
+// RMSNorm + rotate-half RoPE over the whole row (rot == H, KPL = 2): lane gl owns pack gl of the
+// first half and pack gl + G of the second half, which hold exactly each other's rotation
+// partners, so the rotation needs no data from other lanes.  w0/w1: the lane's weights.
+template <typename T, int G>
+__device__ __forceinline__ void rms_rope_half_row(const NormArgs& a, const uint4* srow, const float2* w0,
+                                                  const float2* w1, uint64_t row, uint32_t gl, bool valid) {
+    constexpr int N2 = Pk<T>::N2, P = 2 * N2;
+    float2 f0[N2], f1[N2];
+    Pk<T>::unpack(srow[gl], f0);
+    Pk<T>::unpack(srow[gl + G], f1);
+    float2 acc0 = make_float2(0.f, 0.f), acc1 = acc0;
+#pragma unroll
+    for (int i = 0; i < N2; ++i) {
+        acc0 = __ffma2_rn(f0[i], f0[i], acc0);
+        acc1 = __ffma2_rn(f1[i], f1[i], acc1);
+    }
+    const float s = group_sum<G>((acc0.x + acc0.y) + (acc1.x + acc1.y));
+    const float inv = rsqrtf(fmaf(s, a.inv_h, a.eps));
+    if (!valid) return;
+    const uint32_t pos = a.pos_of_row(static_cast<uint32_t>(row));
+    const size_t t0 = static_cast<size_t>(pos) * (G * P) + gl * P;  // table row of H/2 entries
+    float c[P], z[P];
+    ldg_f32<P>(a.cos_t + t0, c);
+    ldg_f32<P>(a.sin_t + t0, z);
+    const float2 inv2 = make_float2(inv, inv);
+    float2 o0[N2], o1[N2];
+#pragma unroll
+    for (int i = 0; i < N2; ++i) {
+        const float2 y0 = __fmul2_rn(__fmul2_rn(f0[i], inv2), w0[i]);
+        const float2 y1 = __fmul2_rn(__fmul2_rn(f1[i], inv2), w1[i]);
+        const float2 c2 = make_float2(c[2 * i], c[2 * i + 1]), z2 = make_float2(z[2 * i], z[2 * i + 1]);
+        o0[i] = __ffma2_rn(y0, c2, __fmul2_rn(make_float2(-y1.x, -y1.y), z2));  // y c - p s
+        o1[i] = __ffma2_rn(y1, c2, __fmul2_rn(y0, z2));                         // y c + p s
+    }
+    uint4* yrow = reinterpret_cast<uint4*>(static_cast<T*>(a.y) + row * a.H);
+    __stcs(yrow + gl, Pk<T>::pack(o0));
+    __stcs(yrow + gl + G, Pk<T>::pack(o1));
+}
+
+// ---- named barriers of one consumer group (4 warps, 128 threads; ids 1..kGroups) ----
+__device__ __forceinline__ void group_bar_sync(uint32_t id) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kGroupWarps * 32) : "memory");
+}
+// Sums (a, b) over the group's 128 threads with one barrier (2 x kGroupWarps floats at `slot`).
+__device__ __forceinline__ float2 group_reduce2(float a, float b, float* slot, uint32_t id, uint32_t gw, uint32_t lane) {
+    a = group_sum<32>(a);
+    b = group_sum<32>(b);
+    if (lane == 0) {
+        slot[gw] = a;
+        slot[kGroupWarps + gw] = b;
+    }
+    group_bar_sync(id);
+    float2 t = make_float2(0.f, 0.f);
+#pragma unroll
+    for (uint32_t w = 0; w < kGroupWarps; ++w) {
+        t.x += slot[w];
+        t.y += slot[kGroupWarps + w];
+    }
+    return t;
+}
+
+// Row-processing variants of the row-stream kernel.
+enum RowMode : int { kGeneric = 0, kLnFast = 1, kRopeHalfFast = 2 };
+
+template <typename T, NormKind KIND, int G, int MODE = kGeneric, int KPL = 1>
 __global__ void __launch_bounds__(kThreads, 1) rowstream_kernel(NormArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
@@ -367,6 +566,18 @@ __global__ void __launch_bounds__(kThreads, 1) rowstream_kernel(NormArgs a) {
         constexpr uint32_t kRowsPerPass = 32 / G;
         const uint32_t sub = lane / G, gl = lane % G;
         const uint32_t grp = warp / kGroupWarps, gw = warp % kGroupWarps;
+        // kRopeHalfFast: this lane's weights stay in registers for the whole kernel.
+        constexpr int kN2 = Pk<T>::N2;
+        float2 w0[kN2], w1[kN2];
+        if constexpr (MODE == kRopeHalfFast) {
+            float wf[2 * kN2];
+            ldg_f32<2 * kN2>(a.gamma + gl * 2 * kN2, wf);
+#pragma unroll
+            for (int i = 0; i < kN2; ++i) w0[i] = make_float2(wf[2 * i], wf[2 * i + 1]);
+            ldg_f32<2 * kN2>(a.gamma + (gl + G) * 2 * kN2, wf);
+#pragma unroll
+            for (int i = 0; i < kN2; ++i) w1[i] = make_float2(wf[2 * i], wf[2 * i + 1]);
+        }
         for (uint64_t i = grp; grp < a.groups; i += a.groups) {
             const uint64_t t = blockIdx.x + i * gridDim.x;
             if (t >= num_tiles) break;
@@ -380,14 +591,156 @@ __global__ void __launch_bounds__(kThreads, 1) rowstream_kernel(NormArgs a) {
             for (uint32_t rb = gw * kRowsPerPass; rb < nr; rb += kGroupWarps * kRowsPerPass) {
                 const uint32_t rr = rb + sub;
                 const bool valid = rr < nr;
-                process_row<T, KIND, G>(a, reinterpret_cast<const pack<T>*>(tile + (valid ? rr : rb) * row_bytes),
-                                        params, r0 + rr, gl, valid);
+                const uint8_t* srow = tile + (valid ? rr : rb) * row_bytes;
+                if constexpr (MODE == kLnFast)
+                    ln_row_fast<T, G, KPL>(a, reinterpret_cast<const uint4*>(srow), params, r0 + rr, gl, valid);
+                else if constexpr (MODE == kRopeHalfFast)
+                    rms_rope_half_row<T, G>(a, reinterpret_cast<const uint4*>(srow), w0, w1, r0 + rr, gl, valid);
+                else
+                    process_row<T, KIND, G>(a, reinterpret_cast<const pack<T>*>(srow), params, r0 + rr, gl, valid);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->empty[stage]);
         }
     }
     __syncthreads();
+}
+
+// LayerNorm for long rows (H = 1024 * KPL 16-bit elements, or 512 * KPL fp32), direct form:
+// no staging ring.  Each group of 128 threads owns whole rows (rows gg, gg + NG, ... for global
+// group gg of NG); a thread keeps its KPL packs of the current row in registers and issues the
+// streaming loads of its next row before working on the current one, so every group has two
+// rows in flight.  Statistics as in ln_group_row (one pass over deviations from the row's first
+// element, exact centred pass when that shift is far from the mean), combined across the group's
+// four warps through shared memory and a named barrier; the reduction slots alternate by row
+// parity so that a row's first write can never overwrite values of the previous row still being
+// read.  No waits other than those barriers, which every thread of a group reaches the same
+// number of times.
+constexpr uint32_t kDirectGroups = 6;
+
+template <typename T, int KPL>
+__global__ void __launch_bounds__(kDirectGroups * kGroupWarps * 32, 1) ln_direct_kernel(NormArgs a) {
+    constexpr int N2 = Pk<T>::N2, P = 2 * N2, GT = kGroupWarps * 32;
+    extern __shared__ uint8_t smem_raw[];
+    float* params = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    float* red_all = params + a.param_floats;  // kDirectGroups x 2 parities x 4 x kGroupWarps
+    for (uint32_t i = threadIdx.x; i < a.H; i += blockDim.x) {
+        const uint32_t slot = param_slot<P, GT>(i / P, (i % P) / 4) + i % 4;
+        params[slot] = a.gamma[i];
+        params[a.param_stride + slot] = a.beta[i];
+    }
+    __syncthreads();
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const uint32_t grp = warp / kGroupWarps, gw = warp % kGroupWarps, tid = gw * 32 + lane;
+    const uint32_t bar_id = 1 + grp;
+    float* red_grp = red_all + grp * 2 * 4 * kGroupWarps;
+    const uint64_t NG = static_cast<uint64_t>(gridDim.x) * kDirectGroups;
+    const uint4* x = static_cast<const uint4*>(a.x);
+    const uint64_t row_packs = a.H / P;
+
+    const uint16_t* x16 = static_cast<const uint16_t*>(a.x);  // first element of a row (K), any T
+    auto first_elem = [&](uint64_t r) -> float {
+        if constexpr (sizeof(T) == 4) return __uint_as_float(__ldg(reinterpret_cast<const uint32_t*>(a.x) + r * a.H));
+        else {
+            const uint16_t bits = __ldg(x16 + r * a.H);
+            return elem<T>::to_f(*reinterpret_cast<const T*>(&bits));
+        }
+    };
+    uint64_t row = static_cast<uint64_t>(blockIdx.x) * kDirectGroups + grp;
+    uint4 cur[KPL];
+    float Kr = 0.f;
+    if (row < a.rows) {
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) cur[j] = __ldcs(x + row * row_packs + tid + GT * j);
+        Kr = first_elem(row);
+    }
+    for (uint32_t it = 0; row < a.rows; ++it, row += NG) {
+        // prefetch the group's next row (and its first element)
+        uint4 nxt[KPL];
+        float Kn = 0.f;
+        const uint64_t nrow = row + NG;
+        if (nrow < a.rows) {
+#pragma unroll
+            for (int j = 0; j < KPL; ++j) nxt[j] = __ldcs(x + nrow * row_packs + tid + GT * j);
+            Kn = first_elem(nrow);
+        }
+        float* red = red_grp + (it & 1) * 4 * kGroupWarps;
+        const float2 nk = make_float2(-Kr, -Kr);
+        float2 s1 = make_float2(0.f, 0.f), s2 = s1;
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+            float2 f[N2];
+            Pk<T>::unpack(cur[j], f);
+#pragma unroll
+            for (int i = 0; i < N2; ++i) {
+                const float2 d = __fadd2_rn(f[i], nk);
+                s1 = __fadd2_rn(s1, d);
+                s2 = __ffma2_rn(d, d, s2);
+            }
+        }
+        const float2 tot = group_reduce2(s1.x + s1.y, s2.x + s2.y, red, bar_id, gw, lane);
+        const float dm = __fdiv_rn(tot.x, static_cast<float>(a.H));  // mean - K
+        const float mean = __fadd_rn(Kr, dm);
+        float var = fmaxf(__fsub_rn(__fdiv_rn(tot.y, static_cast<float>(a.H)), __fmul_rn(dm, dm)), 0.f);
+        const float2 nmean = make_float2(-mean, -mean);
+        if (dm * dm > 16.f * var) {  // group-uniform: exact centred pass
+            float2 q = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < KPL; ++j) {
+                float2 f[N2];
+                Pk<T>::unpack(cur[j], f);
+#pragma unroll
+                for (int i = 0; i < N2; ++i) {
+                    const float2 d = __fadd2_rn(f[i], nmean);
+                    q = __ffma2_rn(d, d, q);
+                }
+            }
+            var = __fdiv_rn(group_reduce2(q.x + q.y, 0.f, red + 2 * kGroupWarps, bar_id, gw, lane).x,
+                            static_cast<float>(a.H));
+        }
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+        const float2 inv2 = make_float2(inv, inv);
+        uint4* yrow = reinterpret_cast<uint4*>(static_cast<T*>(a.y) + row * a.H);
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+            const uint32_t k = tid + GT * j;
+            float2 f[N2], o[N2];
+            float g[P], b[P];
+            Pk<T>::unpack(cur[j], f);
+            load_params<P, GT>(params, k, g);
+            load_params<P, GT>(params + a.param_stride, k, b);
+#pragma unroll
+            for (int i = 0; i < N2; ++i) {
+                const float2 y = __fmul2_rn(__fadd2_rn(f[i], nmean), inv2);
+                o[i] = __ffma2_rn(y, make_float2(g[2 * i], g[2 * i + 1]), make_float2(b[2 * i], b[2 * i + 1]));
+            }
+            __stcs(yrow + k, Pk<T>::pack(o));
+        }
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) cur[j] = nxt[j];
+        Kr = Kn;
+    }
+}
+
+template <typename T, int KPL>
+int launch_ln_direct(NormArgs a, cudaStream_t s) {
+    constexpr uint32_t P = elem<T>::kPack, GT = kGroupWarps * 32;
+    a.param_stride = a.H / P / GT * GT * P;  // = H: packs are a multiple of GT
+    a.param_floats = 2 * a.param_stride;
+    const size_t smem = 128 + static_cast<size_t>(a.param_floats) * 4 + kDirectGroups * 2 * 4 * kGroupWarps * 4;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(ln_direct_kernel<T, KPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(ln_direct_kernel)");
+        attr_set = true;
+    }
+    const uint64_t groups_needed = (static_cast<uint64_t>(a.rows) + 1) / 2;  // two rows per group at least
+    uint64_t grid = (groups_needed + kDirectGroups - 1) / kDirectGroups;
+    if (grid > static_cast<uint64_t>(sm_count())) grid = sm_count();
+    if (grid == 0) grid = 1;
+    ln_direct_kernel<T, KPL><<<static_cast<unsigned>(grid), kDirectGroups * GT, smem, s>>>(a);
+    return check_launch("layer_norm");
 }
 
 // Scalar fallback (unaligned buffers or rows that are not a multiple of 16 bytes): one block per
@@ -400,11 +753,12 @@ __global__ void __launch_bounds__(256) rownorm_scalar_kernel(NormArgs a) {
     T* y = static_cast<T*>(a.y);
     for (uint64_t row = blockIdx.x; row < a.rows; row += gridDim.x) {
         const T* xr = x + row * a.H;
+        const float K = (KIND == NormKind::kLayerNorm) ? elem<T>::to_f(xr[0]) : 0.f;  // LayerNorm shift
         float s = 0.f;
         for (uint32_t d = threadIdx.x; d < a.H; d += blockDim.x) {
             float v = elem<T>::to_f(xr[d]);
             row_buf[d] = v;
-            s = (KIND == NormKind::kLayerNorm) ? __fadd_rn(s, v) : __fadd_rn(s, __fmul_rn(v, v));
+            s = (KIND == NormKind::kLayerNorm) ? __fadd_rn(s, __fsub_rn(v, K)) : __fadd_rn(s, __fmul_rn(v, v));
         }
         auto block_sum = [&](float v) {
             v = warp_sum(v);
@@ -418,7 +772,7 @@ __global__ void __launch_bounds__(256) rownorm_scalar_kernel(NormArgs a) {
         s = block_sum(s);
         float mul, shift = 0.f;
         if (KIND == NormKind::kLayerNorm) {
-            float mean = __fdiv_rn(s, static_cast<float>(a.H));
+            float mean = __fadd_rn(K, __fdiv_rn(s, static_cast<float>(a.H)));
             float q = 0.f;
             for (uint32_t d = threadIdx.x; d < a.H; d += blockDim.x) {
                 float dd = __fsub_rn(row_buf[d], mean);
@@ -472,7 +826,7 @@ uint32_t read_error_word(const char** name) {
     return word;
 }
 
-template <typename T, NormKind KIND, int G>
+template <typename T, NormKind KIND, int G, int MODE = kGeneric, int KPL = 1>
 int launch_rowstream(NormArgs a, cudaStream_t s) {
     static std::once_flag reg_once;
     std::call_once(reg_once, [] { register_error_word(read_error_word); });
@@ -513,14 +867,14 @@ int launch_rowstream(NormArgs a, cudaStream_t s) {
     const size_t smem = 128 + param_bytes + static_cast<size_t>(a.stages) * a.tile_bytes + bar_bytes;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(rowstream_kernel<T, KIND, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(rowstream_kernel<T, KIND, G, MODE, KPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kSmemBudget + 1024));
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowstream_kernel)");
         attr_set = true;
     }
     const uint64_t tiles = (a.rows + a.tile_rows - 1) / a.tile_rows;
     const uint64_t grid = tiles < static_cast<uint64_t>(sm_count()) ? tiles : static_cast<uint64_t>(sm_count());
-    rowstream_kernel<T, KIND, G><<<static_cast<unsigned>(grid), kThreads, smem, s>>>(a);
+    rowstream_kernel<T, KIND, G, MODE, KPL><<<static_cast<unsigned>(grid), kThreads, smem, s>>>(a);
     return check_launch(KIND == NormKind::kLayerNorm ? "layer_norm" : "rms_norm_rope_fused");
 }
 
@@ -533,6 +887,28 @@ int launch_rownorm(NormArgs a, void* stream) {
     const bool stream_ok = (a.H % P == 0) && aligned16(a.x) && aligned16(a.y) &&
                            a.param_floats * 4ull <= 64 * 1024;
     if (stream_ok) {
+        if constexpr (KIND == NormKind::kLayerNorm) {
+            switch (packs) {  // long rows of 128 * KPL packs: one 128-thread group per row, direct loads
+                case 128: return launch_ln_direct<T, 1>(a, s);
+                case 256: return launch_ln_direct<T, 2>(a, s);
+                case 512: return launch_ln_direct<T, 4>(a, s);
+                default: break;
+            }
+            switch (packs) {  // rows of exactly 32 * KPL packs: the unrolled LayerNorm
+                case 64: return launch_rowstream<T, KIND, 32, kLnFast, 2>(a, s);
+                case 128: return launch_rowstream<T, KIND, 32, kLnFast, 4>(a, s);
+                case 256: return launch_rowstream<T, KIND, 32, kLnFast, 8>(a, s);
+                case 512: return launch_rowstream<T, KIND, 32, kLnFast, 16>(a, s);
+                default: break;
+            }
+        } else {
+            // rotate-half over the whole row with 16-byte-aligned tables: lane-local partners
+            // (weights and tables are read as 16-byte vectors: all three must be 16-byte aligned)
+            const bool half_local = a.style == 1 && a.rot == a.H && aligned16(a.cos_t) && aligned16(a.sin_t) &&
+                                    aligned16(a.gamma) && (a.H / 2) % 4 == 0;
+            if (half_local && packs == 16) return launch_rowstream<T, KIND, 8, kRopeHalfFast, 2>(a, s);
+            if (half_local && packs == 32) return launch_rowstream<T, KIND, 16, kRopeHalfFast, 2>(a, s);
+        }
         if (packs >= 32) return launch_rowstream<T, KIND, 32>(a, s);
         if (packs >= 16) return launch_rowstream<T, KIND, 16>(a, s);
         return launch_rowstream<T, KIND, 8>(a, s);

@@ -241,3 +241,79 @@ def test_rms_norm_rope_config(cuda, hc_lib, oracle):
     for b in range(B):  # oracle per batch keeps host memory bounded
         ref = oracle.rms_norm_rope(quantize(x[b:b + 1], "bf16", oracle), w, cos, sin, D, 1e-6, heads=Hh, style=1)
         assert_close(ref, got[b:b + 1], 2e-2, OUT_HALF_ULP["bf16"], f"rms_norm_rope config batch {b}")
+
+
+# --------------------------------------------------------------------------- unrolled row paths
+@pytest.mark.parametrize("kind", KINDS)
+@pytest.mark.parametrize("dim", [256, 512, 1024, 2048, 4096])
+def test_layer_norm_unrolled_widths(cuda, hc_lib, oracle, kind, dim):
+    """Rows of exactly 32*KPL packs take the unrolled LayerNorm (KPL 2..16); others the generic loop."""
+    rows = 37
+    x = oracle.normal(rows * dim, 11).reshape(rows, dim) * 2.0 + 0.5
+    g = oracle.uniform(dim, 12, 0.5, 1.5)
+    b = oracle.uniform(dim, 13, -0.1, 0.1)
+    y = hc_lib.layer_norm(dev(x, kind, oracle), dev(g, "f32", oracle), dev(b, "f32", oracle), 1e-5)
+    ref = oracle.layer_norm(quantize(x, kind, oracle), g, b, 1e-5)
+    if kind == "f32":
+        assert_close(ref, host(y, oracle), 1e-4, 1e-4, f"layer_norm f32 dim {dim}")
+    else:
+        assert_close(ref, host(y, oracle), 1e-2, OUT_HALF_ULP[kind], f"layer_norm {kind} dim {dim}")
+
+
+@pytest.mark.parametrize("dim", [64, 256, 1024, 4096])
+def test_layer_norm_reference_low_variance_row(cuda, hc_lib, oracle, dim):
+    """test_layer_norm.cpp:91-117: rows base + 1e-6 * d (base 5 and -3), gamma/beta seeds 101/102,
+    tolerance 1e-4 -- at the reference's dim 64 and at widths that take the unrolled paths."""
+    x = np.stack([np.float32(base) + np.float32(1e-6) * np.arange(dim, dtype=np.float32) for base in (5.0, -3.0)])
+    g = oracle.uniform(dim, 101, 0.5, 1.5)
+    b = oracle.uniform(dim, 102, -0.5, 0.5)
+    y = hc_lib.layer_norm(dev(x, "f32", oracle), dev(g, "f32", oracle), dev(b, "f32", oracle), 1e-5)
+    assert_close(oracle.layer_norm(x, g, b, 1e-5), host(y, oracle), 1e-4, 1e-4, f"low variance dim {dim}")
+
+
+def test_layer_norm_low_variance_rows(cuda, hc_lib, oracle):
+    """Large mean, tiny spread (test_layer_norm.cpp:92-117 style): the centred passes keep it accurate."""
+    rows, dim = 8, 1024
+    x = (1000.0 + oracle.uniform(rows * dim, 21, -1e-2, 1e-2)).astype(np.float32).reshape(rows, dim)
+    g = np.ones(dim, np.float32)
+    b = np.zeros(dim, np.float32)
+    y = hc_lib.layer_norm(dev(x, "f32", oracle), dev(g, "f32", oracle), dev(b, "f32", oracle), 1e-5)
+    assert_close(oracle.layer_norm(x, g, b, 1e-5), host(y, oracle), 2e-3, 2e-3, "low variance")
+
+
+@pytest.mark.parametrize("kind", KINDS)
+def test_rms_norm_rope_lane_local_and_unaligned_weight(cuda, hc_lib, oracle, kind):
+    """Rotate-half over the whole row (the lane-local fast path), and the same call with a weight
+    vector that is not 16-byte aligned, which must take the generic path with the same results."""
+    B, S, Hh, H = 3, 65, 4, 128
+    x = oracle.normal(B * S * Hh * H, 31).reshape(B, S, Hh, H)
+    w = oracle.uniform(H + 1, 32, 0.5, 1.5)
+    cos, sin = oracle.rope_cos_sin(S, H // 2)
+    wd = dev(w, "f32", oracle)
+    xd, cd, sd = dev(x, kind, oracle), dev(cos, "f32", oracle), dev(sin, "f32", oracle)
+    tol = (1e-4, 1e-4) if kind == "f32" else (2e-2, OUT_HALF_ULP[kind])
+    for off in (0, 1):
+        wv = wd[off:off + H]
+        assert wv.data_ptr() % 16 == 4 * off
+        out = hc_lib.rms_norm_rope_fused(xd, wv, cd, sd, H, 1e-6, heads=Hh, rope_style=1)
+        ref = oracle.rms_norm_rope(quantize(x, kind, oracle), w[off:off + H], cos, sin, H, 1e-6, heads=Hh, style=1)
+        assert_close(ref, host(out, oracle), *tol, f"{kind} weight offset {off}")
+
+
+@pytest.mark.parametrize("kind", ["f32", "bf16"])
+@pytest.mark.parametrize("dim", [1024, 2048, 4096])
+def test_layer_norm_outlier_first_element(cuda, hc_lib, oracle, kind, dim):
+    """Rows whose first element is far from the mean: the one-pass shifted variance of the
+    group-per-row kernel must fall back to the exact centred pass (alternate rows do)."""
+    rows = 6
+    x = oracle.normal(rows * dim, 41).reshape(rows, dim)
+    x[::2, 0] = 1000.0
+    x[1::2, 0] = -250.0
+    g = oracle.uniform(dim, 42, 0.5, 1.5)
+    b = oracle.uniform(dim, 43, -0.1, 0.1)
+    y = hc_lib.layer_norm(dev(x, kind, oracle), dev(g, "f32", oracle), dev(b, "f32", oracle), 1e-5)
+    ref = oracle.layer_norm(quantize(x, kind, oracle), g, b, 1e-5)
+    if kind == "f32":
+        assert_close(ref, host(y, oracle), 1e-4, 1e-4, f"outlier f32 dim {dim}")
+    else:
+        assert_close(ref, host(y, oracle), 1e-2, OUT_HALF_ULP[kind], f"outlier bf16 dim {dim}")
