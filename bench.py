@@ -147,7 +147,14 @@ class ClockSampler:
 # distributed plumbing (one process per GPU; no collective on the data path)
 # ------------------------------------------------------------------------------------------------
 class Dist:
-    def __init__(self, world: int):
+    """One process per GPU (RANK / WORLD_SIZE / LOCAL_RANK from torchrun).  NCCL carries only the
+    barrier and the max-over-ranks of the timed region; `backend="gloo"` runs the same logic on
+    CPU ranks.  The process-group timeout is short so that ranks waiting for a rank that died end
+    with an error instead of waiting for good."""
+
+    def __init__(self, world: int, backend: str | None = None, timeout_s: float = 120.0):
+        import datetime
+
         import torch
         import torch.distributed as dist
 
@@ -155,12 +162,15 @@ class Dist:
         self.world = int(os.environ.get("WORLD_SIZE", str(world)))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.dist = dist if self.world > 1 else None
+        self.backend = backend or ("nccl" if torch.cuda.is_available() else "gloo")
+        self.device = "cuda" if self.backend == "nccl" else "cpu"
         if self.dist:
-            import datetime
-
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                    device_id=torch.device("cuda", self.local))
+            timeout = datetime.timedelta(seconds=timeout_s)
+            if self.backend == "nccl":
+                torch.cuda.set_device(self.local)
+                dist.init_process_group("nccl", timeout=timeout, device_id=torch.device("cuda", self.local))
+            else:
+                dist.init_process_group(self.backend, timeout=timeout)
 
     def barrier(self):
         if self.dist:
@@ -171,7 +181,7 @@ class Dist:
             return v
         import torch
 
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        t = torch.tensor([v], dtype=torch.float64, device=self.device)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
@@ -179,6 +189,12 @@ class Dist:
         if self.dist:
             self.dist.barrier()
             self.dist.destroy_process_group()
+
+
+def whole_job_rate(units_per_rank: float, world: int, ms_max: float) -> float:
+    """Weak scaling: every rank processes `units_per_rank`; the job's rate is all ranks' units
+    divided by the slowest rank's time (units per second)."""
+    return world * units_per_rank / (ms_max * 1e-3)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -341,7 +357,7 @@ def run_ours(args):
     hc.check_device_error()
     ms = d.max(ms_local)
     flops_rank = fa_flops(fa_b, FA_H, FA_S, FA_S, FA_D, True)
-    value = n * flops_rank / (ms * 1e-3) / 1e12
+    value = whole_job_rate(flops_rank, n, ms) / 1e12
     achieved = flops_rank / (ms_local * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops"],

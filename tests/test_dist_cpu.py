@@ -1,0 +1,78 @@
+"""Multi-rank logic of bench.py on CPU ranks (gloo, world size 2): the barrier, the max over ranks
+of the timed region, the whole-job rate from the slowest rank, and that a rank which dies before
+the barrier makes the other rank fail with an error (short process-group timeout) instead of
+waiting for good.  No GPU."""
+from __future__ import annotations
+
+import multiprocessing as mp
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    sys.path.insert(0, str(ROOT))
+    try:
+        import bench
+
+        d = bench.Dist(world, backend="gloo", timeout_s=10.0)
+        if mode == "die" and rank == 1:
+            os._exit(3)  # leaves between steps, without joining the barrier
+        d.barrier()
+        ms_local = 10.0 + 5.0 * rank  # rank 1 is the slow one
+        ms = d.max(ms_local)
+        rate = bench.whole_job_rate(1.0e9, d.world, ms)
+        d.close()
+        q.put((rank, "ok", ms, rate))
+    except Exception as e:  # noqa: BLE001 -- reported to the parent
+        q.put((rank, "error", type(e).__name__, str(e)[:200]))
+
+
+def _run(world: int, mode: str, timeout: float):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+        p.join()
+    out = []
+    while not q.empty():
+        out.append(q.get())
+    return out, alive
+
+
+def test_two_gloo_ranks_take_max_and_aggregate():
+    out, alive = _run(2, "ok", 120)
+    assert not alive
+    res = {r[0]: r for r in out}
+    assert set(res) == {0, 1}, out
+    for r in (0, 1):
+        assert res[r][1] == "ok", res[r]
+        assert res[r][2] == pytest.approx(15.0)                  # max over ranks, on every rank
+        assert res[r][3] == pytest.approx(2 * 1.0e9 / 15.0e-3)   # both ranks' work / slowest time
+
+
+def test_dead_rank_makes_the_other_fail_not_hang():
+    out, alive = _run(2, "die", 90)
+    assert not alive, "a rank waited for good on a rank that died"
+    res = {r[0]: r for r in out}
+    assert 0 in res and res[0][1] == "error", out
