@@ -435,14 +435,23 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
     steps, warm = 20, 3
     # The bandwidth workloads below each read more than the 126 MB L2 per launch (layer_norm
     # 134 MB, rms_norm_rope 268 MB, elementwise_add 134 MB), so they run back to back without an
-    # L2 flush: a launch finds at most the previous launch's tail in L2.
+    # L2 flush; consecutive launches alternate between two independent buffer sets, so a launch
+    # can neither re-read the previous launch's inputs nor rewrite its still-dirty outputs in L2.
     hbm = peaks["hbm_gbs"]
+    flip = [0]
+
+    def alternate(sets):
+        def nxt():
+            flip[0] ^= 1
+            return sets[flip[0]]
+        return nxt
     g = torch.Generator(device=dev).manual_seed(0)
 
     def bw_entry(name, bytes_, ms, launches=1):
         gbs = bytes_ / (ms * 1e-3) / 1e9
         out[name] = {"value": d.world * gbs, "unit": "GB/s", "per_gpu": gbs, "ms": ms,
-                     "timing": f"{steps} back-to-back launches, no L2 flush (each reads > 126 MB)",
+                     "timing": f"{steps} back-to-back launches alternating two buffer sets, no L2 flush "
+                               "(each reads > 126 MB)",
                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                                   "algorithmic_bytes_per_launch": bytes_, "traffic": profile_traffic(name)}}
 
@@ -477,33 +486,51 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
         del A, B, bias, C
 
     if "layer_norm" in want:  # [16384, 4096] bf16, fp32 gamma/beta
-        x = torch.randn((16384, 4096), generator=g, device=dev).to(torch.bfloat16)
         gamma = torch.rand((4096,), generator=g, device=dev) + 0.5
         beta = torch.rand((4096,), generator=g, device=dev) * 0.2 - 0.1
-        y = torch.empty_like(x)
-        ms = time_launches(lambda: hc.layer_norm(x, gamma, beta, 1e-5, y=y), steps, warm, d)
+        sets = []
+        for _ in range(2):
+            x = torch.randn((16384, 4096), generator=g, device=dev).to(torch.bfloat16)
+            sets.append((x, torch.empty_like(x)))
+        nxt = alternate(sets)
+
+        def ln_step():
+            xx, yy = nxt()
+            hc.layer_norm(xx, gamma, beta, 1e-5, y=yy)
+
+        ms = time_launches(ln_step, steps, warm, d)
         bw_entry("layer_norm", 2 * x.numel() * 2 + 2 * 4096 * 4, ms)
-        del x, y
+        del x, sets
 
     if "rms_norm_rope_fused" in want:  # [8, 4096, 32, 128] bf16, rotate-half, fp32 cos/sin [4096, 64]
-        x = torch.randn((8, 4096, 32, 128), generator=g, device=dev).to(torch.bfloat16)
         w = torch.rand((128,), generator=g, device=dev) + 0.5
         pos = torch.arange(4096, device=dev, dtype=torch.float32)[:, None]
         inv = 1.0 / (10000.0 ** (torch.arange(64, device=dev, dtype=torch.float32) * 2 / 128))
         cos, sin = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
-        y = torch.empty_like(x)
-        ms = time_launches(lambda: hc.rms_norm_rope_fused(x, w, cos, sin, 128, 1e-6, heads=32, rope_style=1, out=y),
-                           steps, warm, d)
+        sets = []
+        for _ in range(2):
+            x = torch.randn((8, 4096, 32, 128), generator=g, device=dev).to(torch.bfloat16)
+            sets.append((x, torch.empty_like(x)))
+        nxt = alternate(sets)
+
+        def rms_step():
+            xx, yy = nxt()
+            hc.rms_norm_rope_fused(xx, w, cos, sin, 128, 1e-6, heads=32, rope_style=1, out=yy)
+
+        ms = time_launches(rms_step, steps, warm, d)
         bw_entry("rms_norm_rope_fused", 2 * x.numel() * 2 + 128 * 4 + 2 * cos.numel() * 4, ms)
-        del x, y
+        del x, sets
 
     if "elementwise_add" in want:  # fp16 [4096, 8192], U[-1, 1]
-        a = (torch.rand((4096, 8192), generator=g, device=dev) * 2 - 1).to(torch.float16)
-        b = (torch.rand((4096, 8192), generator=g, device=dev) * 2 - 1).to(torch.float16)
-        z = torch.empty_like(a)
-        ms = time_launches(lambda: hc.elementwise_add(a, b, z), steps, warm, d)
+        sets = []
+        for _ in range(2):
+            a = (torch.rand((4096, 8192), generator=g, device=dev) * 2 - 1).to(torch.float16)
+            b = (torch.rand((4096, 8192), generator=g, device=dev) * 2 - 1).to(torch.float16)
+            sets.append((a, b, torch.empty_like(a)))
+        nxt = alternate(sets)
+        ms = time_launches(lambda: hc.elementwise_add(*nxt()), steps, warm, d)
         bw_entry("elementwise_add", 3 * a.numel() * 2, ms)
-        del a, b, z
+        del a, b, sets
     torch.cuda.empty_cache()
     return out
 
