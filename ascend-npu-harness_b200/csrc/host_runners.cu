@@ -158,3 +158,112 @@ extern "C" int hc_flash_attention_fwd_fused_host(const void* h_q, const void* h_
     HC_CHECK_CUDA(cudaStreamSynchronize(P.out));
     return hc_check_device_error();
 }
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free variant of the host-buffer flash-attention runner.
+//
+// Staging memory is a file-scope device array instead of a caller workspace, so the call makes
+// no device allocation of any kind (no cudaMalloc / cudaFree, no allocating library routine) and
+// creates no streams or events: everything runs in order on the caller's stream, one chunk of
+// whole heads at a time (copy in, kernel, copy out).  For callers whose device memory is entirely
+// owned by their own pool or budget, where an allocation inside the call could fail or would
+// synchronise the device.
+//   * Limit: kNoAllocScratchBytes per device.  One head's staging (q, k, v, o, lse) must fit;
+//     larger heads are rejected with HC_ERR_UNSUPPORTED before any device work.
+//   * The first call on a device looks the array's address up with cudaGetSymbolAddress (and
+//     the kernel sets its attributes); make that first call before any stream capture.
+//   * Nothing in the scratch has to start at zero: every byte read is written earlier in the
+//     same call.
+//   * All calls on one device share the one array: calls that overlap in time (other threads,
+//     other streams) race on it and must be serialised by the caller.
+// ------------------------------------------------------------------------------------------
+namespace hc {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 64ull << 20;  // 64 MiB per device
+static __device__ __align__(256) uint8_t g_fa_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    HC_CHECK_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(HC_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_fa_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(flash-attention scratch)");
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return HC_OK;
+}
+
+// Staging bytes of `h` consecutive heads: q, k, v, o, lse, each 256-byte aligned.
+uint64_t noalloc_chunk_bytes(const flash_attention_fwd_fused_tiling_data* t, size_t es, uint64_t h) {
+    auto align = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
+    return align(h * t->S_q * t->D * es) + align(h * static_cast<uint64_t>(t->S_k) * t->D * es) +
+           align(h * static_cast<uint64_t>(t->S_k) * t->D_v * es) + align(h * t->S_q * t->D_v * es) +
+           align(h * t->S_q * sizeof(float));
+}
+
+}  // namespace
+}  // namespace hc
+
+extern "C" size_t hc_flash_attention_fwd_fused_host_noalloc_limit(void) { return hc::kNoAllocScratchBytes; }
+
+extern "C" int hc_flash_attention_fwd_fused_host_noalloc(const void* h_q, const void* h_k, const void* h_v, void* h_o,
+                                                         float* h_lse, const flash_attention_fwd_fused_tiling_data* t,
+                                                         int dtype, void* stream) {
+    if (!t) return fail(HC_ERR_INVALID, "flash_attention host (no-alloc): null tiling");
+    if (!h_q || !h_k || !h_v || !h_o) return fail(HC_ERR_INVALID, "flash_attention host (no-alloc): null pointer");
+    const size_t es = dtype_size(dtype);
+    if (dtype != HC_DTYPE_F32 && dtype != HC_DTYPE_F16 && dtype != HC_DTYPE_BF16)
+        return fail(HC_ERR_UNSUPPORTED, "flash_attention host (no-alloc): dtype %d", dtype);
+    const uint64_t bh = static_cast<uint64_t>(t->B) * t->H;
+    if (bh == 0 || t->S_q == 0) return ok();
+    if (noalloc_chunk_bytes(t, es, 1) > kNoAllocScratchBytes)
+        return fail(HC_ERR_UNSUPPORTED,
+                    "flash_attention host (no-alloc): one head needs %llu B of staging, above the %zu B scratch",
+                    static_cast<unsigned long long>(noalloc_chunk_bytes(t, es, 1)), kNoAllocScratchBytes);
+    uint64_t h = kNoAllocScratchBytes / noalloc_chunk_bytes(t, es, 1);
+    if (h > bh) h = bh;
+    while (h > 1 && noalloc_chunk_bytes(t, es, h) > kNoAllocScratchBytes) --h;
+    void* scratch = nullptr;
+    int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    auto align = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
+    const uint64_t q_h = static_cast<uint64_t>(t->S_q) * t->D * es;
+    const uint64_t k_h = static_cast<uint64_t>(t->S_k) * t->D * es;
+    const uint64_t v_h = static_cast<uint64_t>(t->S_k) * t->D_v * es;
+    const uint64_t o_h = static_cast<uint64_t>(t->S_q) * t->D_v * es;
+    const uint64_t l_h = static_cast<uint64_t>(t->S_q) * sizeof(float);
+    uint8_t* dq = static_cast<uint8_t*>(scratch);
+    uint8_t* dk = dq + align(h * q_h);
+    uint8_t* dv = dk + align(h * k_h);
+    uint8_t* dO = dv + align(h * v_h);
+    float* dl = reinterpret_cast<float*>(dO + align(h * o_h));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (uint64_t h0 = 0; h0 < bh; h0 += h) {
+        const uint64_t hn = (h0 + h <= bh) ? h : (bh - h0);
+        HC_CHECK_CUDA(cudaMemcpyAsync(dq, static_cast<const uint8_t*>(h_q) + h0 * q_h, hn * q_h,
+                                      cudaMemcpyHostToDevice, s));
+        HC_CHECK_CUDA(cudaMemcpyAsync(dk, static_cast<const uint8_t*>(h_k) + h0 * k_h, hn * k_h,
+                                      cudaMemcpyHostToDevice, s));
+        HC_CHECK_CUDA(cudaMemcpyAsync(dv, static_cast<const uint8_t*>(h_v) + h0 * v_h, hn * v_h,
+                                      cudaMemcpyHostToDevice, s));
+        flash_attention_fwd_fused_tiling_data tc = *t;
+        tc.B = 1;
+        tc.H = static_cast<uint32_t>(hn);
+        rc = hc_flash_attention_fwd_fused_launch(dq, dk, dv, dO, h_lse ? dl : nullptr, &tc, dtype, s);
+        if (rc) return rc;
+        HC_CHECK_CUDA(cudaMemcpyAsync(static_cast<uint8_t*>(h_o) + h0 * o_h, dO, hn * o_h, cudaMemcpyDeviceToHost, s));
+        if (h_lse)
+            HC_CHECK_CUDA(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(h_lse) + h0 * l_h, dl, hn * l_h,
+                                          cudaMemcpyDeviceToHost, s));
+    }
+    HC_CHECK_CUDA(cudaStreamSynchronize(s));
+    return hc_check_device_error();
+}

@@ -131,6 +131,9 @@ SIGNATURES = {
     "hc_flash_attention_fwd_fused_host_workspace_size": (_i, [_P(FlashAttentionFwdFusedTiling), _i, _P(_sz)]),
     "hc_flash_attention_fwd_fused_host": (_i, [_vp, _vp, _vp, _vp, _vp, _P(FlashAttentionFwdFusedTiling), _i, _vp,
                                                _sz, _vp]),
+    "hc_flash_attention_fwd_fused_host_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _P(FlashAttentionFwdFusedTiling),
+                                                       _i, _vp]),
+    "hc_flash_attention_fwd_fused_host_noalloc_limit": (_sz, []),
     "hc_flash_attention_last_path": (_i, []),
     "hc_matmul_bias_last_path": (_i, []),
 }

@@ -217,6 +217,26 @@ int hc_flash_attention_fwd_fused_host(const void* h_q, const void* h_k, const vo
                                       int dtype, void* workspace, size_t workspace_bytes,
                                       void* stream);
 
+/* Allocation-free variant of hc_flash_attention_fwd_fused_host (no counterpart in the reference):
+ * the device staging memory is a fixed scratch array inside this library, so the call allocates
+ * no device memory (no cudaMalloc / cudaFree, no allocating library routine) and creates no
+ * streams or events.  It is meant for callers that cannot allocate on this path, such as a
+ * serving loop whose device memory is fully reserved by its own pool, where an allocation could
+ * fail or would synchronise the device.  Copies and kernels run in order on `stream`, one chunk
+ * of whole heads at a time (no copy/compute overlap); returns when h_o / h_lse hold the result.
+ *   Limit: hc_flash_attention_fwd_fused_host_noalloc_limit() bytes (64 MiB) of staging per
+ *   device; a head whose q, k, v, o and lse do not fit is rejected with HC_ERR_UNSUPPORTED
+ *   before any device work.
+ *   The first call on a device does one-time setup (the scratch's address is looked up with
+ *   cudaGetSymbolAddress, the kernel sets its attributes): make it before any stream capture.
+ *   Nothing in the scratch needs to start at zero.  Calls that overlap in time on one device
+ *   (other threads or streams) race on the single scratch array and must be serialised. */
+int hc_flash_attention_fwd_fused_host_noalloc(const void* h_q, const void* h_k, const void* h_v, void* h_o,
+                                              float* h_lse,
+                                              const struct flash_attention_fwd_fused_tiling_data* t,
+                                              int dtype, void* stream);
+size_t hc_flash_attention_fwd_fused_host_noalloc_limit(void);
+
 /* Kernel selection used by the last successful flash-attention / matmul_bias launch on this
  * thread: 1 = tcgen05/TMEM path, 2 = SIMT path, 0 = none yet. */
 int hc_flash_attention_last_path(void);

@@ -101,3 +101,18 @@ def test_python_binding_raises_on_error(hc_lib):
     with pytest.raises(hc_lib.HcError) as ei:
         hc_lib.check(hc_lib.HC_ERR_INVALID)
     assert ei.value.status == hc_lib.HC_ERR_INVALID
+
+
+def test_noalloc_runner_limits_are_checked_on_the_host(hc_lib):
+    """The allocation-free runner rejects a head larger than its fixed scratch before any device work."""
+    lib = hc_lib.load()
+    assert lib.hc_flash_attention_fwd_fused_host_noalloc_limit() == 64 << 20
+    fake = C.c_void_p(0x1000)
+    big = hc_lib.FlashAttentionFwdFusedTiling(1, 1, 1 << 20, 1 << 20, 128, 128, 0.088, 1)  # one head: 1 GiB
+    assert lib.hc_flash_attention_fwd_fused_host_noalloc(fake, fake, fake, fake, None, C.byref(big), 2, None) \
+        == hc_lib.HC_ERR_UNSUPPORTED
+    assert "scratch" in hc_lib.load().hc_last_error_string().decode()
+    assert lib.hc_flash_attention_fwd_fused_host_noalloc(None, fake, fake, fake, None, C.byref(big), 2, None) \
+        == hc_lib.HC_ERR_INVALID
+    assert lib.hc_flash_attention_fwd_fused_host_noalloc(fake, fake, fake, fake, None, C.byref(big), 3, None) \
+        == hc_lib.HC_ERR_UNSUPPORTED
