@@ -9,6 +9,7 @@
 //   axpy_scalar_affine   ops/axpy_scalar_affine/golden/axpy_scalar_affine_golden.cpp:13-15
 //   broadcast_binary     ops/broadcast_binary/golden/broadcast_binary_golden.cpp:28-40
 //   activation_gelu_silu ops/activation_gelu_silu/golden/activation_gelu_silu_golden.cpp:16-49
+//                        (fp32; bf16/fp16 use the sigmoid form of FastActOp, see there)
 #include <cuda_runtime.h>
 
 #include "hc_device.cuh"
@@ -120,6 +121,21 @@ struct ActOp {
     }
 };
 
+// 16-bit outputs: the same functions through the logistic sigmoid, which needs one exponential
+// and one approximate reciprocal instead of tanhf / expf / IEEE division:
+//   GELU_tanh(x) = 0.5 x (1 + tanh u) = x * sigmoid(2u),  u = sqrt(2/pi) (x + 0.044715 x^3);
+//   SiLU(x) = x * sigmoid(x);  sigmoid(z) = 1 / (1 + e^-z).
+// Relative error ~1e-6, far below the rounding of the bf16/fp16 result (2^-9 / 2^-12); the fp32
+// path (ActOp) keeps the golden's operation order.  For z -> -inf, e^-z = inf and x / inf = 0.
+struct FastActOp {
+    static constexpr bool kBinary = false;
+    uint32_t act;  // 0 = GELU (tanh form), 1 = SiLU
+    __device__ float apply(float v, float) const {
+        const float z = (act == 0) ? 1.5957691216f * fmaf(0.044715f * v, v * v, v) : v;  // 2 sqrt(2/pi) = 1.5957691216
+        return __fdividef(v, 1.0f + __expf(-z));
+    }
+};
+
 template <typename T, typename Op>
 int launch_map(const void* a, const void* b, void* out, size_t n, Op op, void* stream, const char* name) {
     if (n == 0) return ok();
@@ -150,23 +166,41 @@ int dispatch_map(int dtype, const void* a, const void* b, void* out, size_t n, O
 // ---------------------------------------------------------------------------------------
 // broadcast_binary: z = x * y[yb, c] + bias[c]
 // ---------------------------------------------------------------------------------------
+// One pack never straddles two (b, c) planes (hw % P == 0).  Pack i lies in plane i / (hw / P);
+// the plane splits into (b, c) = (plane / C, plane % C), both by multiply-shift division (the
+// launcher takes this kernel only when the pack count fits 32 bits).
 template <typename T>
 __global__ void __launch_bounds__(kThreads) broadcast_vec_kernel(const T* __restrict__ x, const T* __restrict__ y,
                                                                  const T* __restrict__ bias, T* __restrict__ z,
-                                                                 uint32_t C, size_t hw, size_t chw, bool y_per_batch,
-                                                                 size_t n) {
+                                                                 FastDiv plane_packs, FastDiv cdiv, bool y_per_batch,
+                                                                 uint32_t packs) {
     constexpr int P = elem<T>::kPack;
-    const size_t packs = n / P;
-    const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+    const uint32_t stride = gridDim.x * blockDim.x;
     const pack<T>* px = reinterpret_cast<const pack<T>*>(x);
     pack<T>* pz = reinterpret_cast<pack<T>*>(z);
-    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < packs; i += stride) {
-        size_t e0 = i * P;  // hw % P == 0, so the whole pack lies in one (b, c) plane
-        size_t b = e0 / chw;
-        uint32_t c = static_cast<uint32_t>((e0 / hw) % C);
-        float yv = elem<T>::to_f(y[(y_per_batch ? b * C : 0) + c]);
-        float bv = elem<T>::to_f(bias[c]);
-        pack<T> v = ld_stream(px + i);
+    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    for (; static_cast<uint64_t>(i) + (kUnroll - 1) * static_cast<uint64_t>(stride) < packs; i += kUnroll * stride) {
+        pack<T> v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) v[u] = ld_stream(px + i + u * stride);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const uint32_t plane = plane_packs.div(i + u * stride);
+            const uint32_t b = cdiv.div(plane), c = plane - b * cdiv.d;
+            const float yv = elem<T>::to_f(y[(y_per_batch ? b * cdiv.d : 0) + c]);
+            const float bv = elem<T>::to_f(bias[c]);
+            pack<T> r;
+#pragma unroll
+            for (int e = 0; e < P; ++e) r.v[e] = elem<T>::from_f(__fadd_rn(__fmul_rn(elem<T>::to_f(v[u].v[e]), yv), bv));
+            st_stream(pz + i + u * stride, r);
+        }
+    }
+    for (; i < packs; i += stride) {
+        const pack<T> v = ld_stream(px + i);
+        const uint32_t plane = plane_packs.div(i);
+        const uint32_t b = cdiv.div(plane), c = plane - b * cdiv.d;
+        const float yv = elem<T>::to_f(y[(y_per_batch ? b * cdiv.d : 0) + c]);
+        const float bv = elem<T>::to_f(bias[c]);
         pack<T> r;
 #pragma unroll
         for (int e = 0; e < P; ++e) r.v[e] = elem<T>::from_f(__fadd_rn(__fmul_rn(elem<T>::to_f(v.v[e]), yv), bv));
@@ -201,8 +235,13 @@ int launch_broadcast(const void* x, const void* y, const void* bias, void* z, co
     const T* ty = static_cast<const T*>(y);
     const T* tb = static_cast<const T*>(bias);
     T* tz = static_cast<T*>(z);
-    if (aligned16(x) && aligned16(z) && hw % elem<T>::kPack == 0) {
-        broadcast_vec_kernel<T><<<grid_for(n / elem<T>::kPack), kThreads, 0, s>>>(tx, ty, tb, tz, t->C, hw, chw, per_batch, n);
+    const size_t packs = n / elem<T>::kPack;
+    if (aligned16(x) && aligned16(z) && hw % elem<T>::kPack == 0 && packs < (1ull << 32) - kThreads * kUnroll * 8ull * 1024) {
+        FastDiv plane_packs, cdiv;
+        plane_packs.init(static_cast<uint32_t>(hw / elem<T>::kPack));
+        cdiv.init(t->C);
+        broadcast_vec_kernel<T><<<grid_for(packs), kThreads, 0, s>>>(tx, ty, tb, tz, plane_packs, cdiv, per_batch,
+                                                                     static_cast<uint32_t>(packs));
     } else {
         broadcast_scalar_kernel<T><<<grid_for(n), kThreads, 0, s>>>(tx, ty, tb, tz, t->C, hw, chw, per_batch, n);
     }
@@ -236,7 +275,9 @@ extern "C" int hc_activation_gelu_silu_launch(const void* x, void* y, const acti
     if (t->actType > 1) return fail(HC_ERR_INVALID, "activation_gelu_silu: actType %u (0 = GELU, 1 = SiLU)", t->actType);
     if (t->totalLength && (!x || !y)) return fail(HC_ERR_INVALID, "activation_gelu_silu: null pointer");
     if (fault_hit("launch")) return fail(HC_ERR_INJECTED, "activation_gelu_silu: injected launch failure");
-    return dispatch_map(dtype, x, nullptr, y, t->totalLength, ActOp{t->actType}, stream, "activation_gelu_silu");
+    if (dtype == HC_DTYPE_F32)
+        return dispatch_map(dtype, x, nullptr, y, t->totalLength, ActOp{t->actType}, stream, "activation_gelu_silu");
+    return dispatch_map(dtype, x, nullptr, y, t->totalLength, FastActOp{t->actType}, stream, "activation_gelu_silu");
 }
 
 extern "C" int hc_broadcast_binary_launch(const void* x, const void* y, const void* bias, void* z,

@@ -140,6 +140,100 @@ __global__ void __launch_bounds__(kTile * kRowsPerPass) transpose_kernel(const E
     }
 }
 
+// 2-byte elements: 64 x 64 tiles, so that every warp access is one 128-byte row segment (a 32 x 32
+// tile of 2-byte elements would move 64-byte segments).  A lane moves two neighbouring elements
+// as one 32-bit word (two 16-bit accesses where a word would be misaligned or cross the edge).
+// Shared-memory rows are 65 elements long: the transposed reads (rows 2l and 2l+1 of one column)
+// then fall on 32 different banks.
+constexpr int kT16 = 64;
+
+__global__ void __launch_bounds__(kTile * kRowsPerPass) transpose16_kernel(const uint16_t* __restrict__ in,
+                                                                           uint16_t* __restrict__ out, uint32_t batch,
+                                                                           uint32_t R, uint32_t C) {
+    constexpr int kRowsPerThread = kT16 / kRowsPerPass;  // 8
+    __shared__ uint16_t tile[kT16][kT16 + 1];
+    const uint64_t tiles_r = (R + kT16 - 1) / kT16;
+    const uint64_t tiles_c = (C + kT16 - 1) / kT16;
+    const uint64_t per_batch = tiles_r * tiles_c;
+    const uint64_t total = per_batch * batch;
+    const size_t mat = static_cast<size_t>(R) * C;
+    const uint32_t l2 = 2 * threadIdx.x;
+    // The tile's rows r0+i (i = threadIdx.y + 8k) are fetched into registers one tile ahead, so
+    // the loads of tile t+1 are in flight while tile t is written out.
+    struct Coord {
+        uint64_t b;
+        uint32_t r0, c0;
+    };
+    auto coord = [&](uint64_t t) {
+        const uint64_t rem = t % per_batch;
+        return Coord{t / per_batch, static_cast<uint32_t>(rem / tiles_c) * kT16, static_cast<uint32_t>(rem % tiles_c) * kT16};
+    };
+    // A 32-bit access needs an even element offset from the 4-byte aligned buffer start: the
+    // parity is that of the batch base b * mat plus the offset inside the matrix.
+    auto fetch = [&](const Coord& k, uint32_t (&w)[kRowsPerThread]) {
+        const uint16_t* src = in + k.b * mat;
+        const size_t base_par = (k.b * mat) & 1;
+#pragma unroll
+        for (int q = 0; q < kRowsPerThread; ++q) {
+            const uint32_t r = k.r0 + threadIdx.y + q * kRowsPerPass, c = k.c0 + l2;
+            uint32_t v = 0;
+            if (r < R) {
+                const size_t o = static_cast<size_t>(r) * C + c;
+                if (c + 1 < C && ((base_par + o) & 1) == 0) {
+                    v = __ldcs(reinterpret_cast<const unsigned int*>(src + o));
+                } else {
+                    if (c < C) v = src[o];
+                    if (c + 1 < C) v |= static_cast<uint32_t>(src[o + 1]) << 16;
+                }
+            }
+            w[q] = v;
+        }
+    };
+    uint32_t w[kRowsPerThread];
+    uint64_t t = blockIdx.x;
+    if (t < total) fetch(coord(t), w);
+    for (; t < total; t += gridDim.x) {
+        const Coord k = coord(t);
+#pragma unroll
+        for (int q = 0; q < kRowsPerThread; ++q) {
+            const int i = threadIdx.y + q * kRowsPerPass;
+            tile[i][l2] = static_cast<uint16_t>(w[q]);
+            tile[i][l2 + 1] = static_cast<uint16_t>(w[q] >> 16);
+        }
+        __syncthreads();
+        if (t + gridDim.x < total) fetch(coord(t + gridDim.x), w);
+        // Rows c0.. of the output, two elements per lane.
+        uint16_t* dst = out + k.b * mat;
+        const size_t base_par = (k.b * mat) & 1;
+#pragma unroll
+        for (int q = 0; q < kRowsPerThread; ++q) {
+            const int i = threadIdx.y + q * kRowsPerPass;
+            const uint32_t c = k.c0 + i, r = k.r0 + l2;
+            if (c >= C) continue;
+            const size_t o = static_cast<size_t>(c) * R + r;
+            const uint16_t lo = tile[l2][i], hi = tile[l2 + 1][i];
+            if (r + 1 < R && ((base_par + o) & 1) == 0) {
+                __stcs(reinterpret_cast<unsigned int*>(dst + o),
+                       static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16));
+            } else {
+                if (r < R) dst[o] = lo;
+                if (r + 1 < R) dst[o + 1] = hi;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+int launch_transpose16(const void* src, void* dst, uint32_t batch, uint32_t R, uint32_t C, void* stream) {
+    const uint64_t tiles = static_cast<uint64_t>((R + kT16 - 1) / kT16) * ((C + kT16 - 1) / kT16) * batch;
+    const uint64_t cap = static_cast<uint64_t>(sm_count()) * 8;
+    const int blocks = static_cast<int>(tiles < cap ? tiles : cap);
+    if (blocks == 0) return ok();
+    transpose16_kernel<<<blocks, dim3(kTile, kRowsPerPass), 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), batch, R, C);
+    return check_launch("transpose_2d_4d");
+}
+
 template <typename E>
 int launch_transpose(const void* src, void* dst, uint32_t batch, uint32_t R, uint32_t C, void* stream) {
     uint64_t tiles = static_cast<uint64_t>((R + kTile - 1) / kTile) * ((C + kTile - 1) / kTile) * batch;
@@ -191,7 +285,10 @@ extern "C" int hc_transpose_2d_4d_launch(const void* src, void* dst, const trans
     if (fault_hit("launch")) return fail(HC_ERR_INJECTED, "transpose_2d_4d: injected launch failure");
     switch (es) {
         case 1: return launch_transpose<uint8_t>(src, dst, batch, R, C, stream);
-        case 2: return launch_transpose<uint16_t>(src, dst, batch, R, C, stream);
+        case 2:
+            if ((reinterpret_cast<uintptr_t>(src) & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 3) == 0)
+                return launch_transpose16(src, dst, batch, R, C, stream);
+            return launch_transpose<uint16_t>(src, dst, batch, R, C, stream);
         default: return launch_transpose<uint32_t>(src, dst, batch, R, C, stream);
     }
 }

@@ -422,7 +422,12 @@ def run_ours(args):
     d.close()
 
 
-EXTRA_OPS = ("flash_attention_fwd_noncausal", "matmul_bias", "layer_norm", "rms_norm_rope_fused", "elementwise_add")
+EXTRA_OPS = ("flash_attention_fwd_noncausal", "matmul_bias", "layer_norm", "rms_norm_rope_fused", "elementwise_add",
+             "axpy_scalar_affine", "broadcast_binary", "activation_gelu_silu", "reduce_sum_lastdim", "transpose_2d_4d")
+# The last five ops have no configuration of their own in the reference's benchmark list; they are
+# timed on sized analogs of the layer_norm shape (134 MB of 16-bit input per launch), stated in
+# each entry's "config".
+ANALOG_OPS = EXTRA_OPS[5:]
 
 
 def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
@@ -531,7 +536,60 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
         ms = time_launches(lambda: hc.elementwise_add(*nxt()), steps, warm, d)
         bw_entry("elementwise_add", 3 * a.numel() * 2, ms)
         del a, b, sets
+    if any(op in want for op in ANALOG_OPS):
+        out.update(run_analogs(hc, d, dev, peaks, want, steps, warm, alternate))
     torch.cuda.empty_cache()
+    return out
+
+
+def run_analogs(hc, d: Dist, dev, peaks, want, steps, warm, alternate) -> dict:
+    """Sized analogs for the ops without a configuration of their own: bf16, 134 MB of input."""
+    import torch
+
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(7)
+    hbm = peaks["hbm_gbs"]
+    R, K = 16384, 4096  # the layer_norm shape
+
+    def rnd(*shape):
+        return torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
+
+    def entry(name, config, bytes_, make_set, run):
+        sets = [make_set() for _ in range(2)]
+        nxt = alternate(sets)
+        ms = time_launches(lambda: run(*nxt()), steps, warm, d)
+        gbs = bytes_ / (ms * 1e-3) / 1e9
+        out[name] = {"value": d.world * gbs, "unit": "GB/s", "per_gpu": gbs, "ms": ms, "config": config,
+                     "timing": f"{steps} back-to-back launches alternating two buffer sets, no L2 flush",
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                                  "algorithmic_bytes_per_launch": bytes_, "traffic": None}}
+
+    n = R * K
+    if "axpy_scalar_affine" in want:
+        entry("axpy_scalar_affine", f"analog: bf16 [{R}, {K}], y = 0.5 x - 1", 2 * n * 2,
+              lambda: (rnd(R, K), torch.empty((R, K), dtype=torch.bfloat16, device=dev)),
+              lambda x, y: hc.axpy_scalar_affine(x, 0.5, -1.0, y=y))
+    if "broadcast_binary" in want:
+        B, Cc, H, W = 16, 256, 128, 128
+        y_ = rnd(B, Cc)
+        bias = rnd(Cc)
+        entry("broadcast_binary", f"analog: bf16 x [{B}, {Cc}, {H}, {W}] NCHW, y [{B}, {Cc}], bias [{Cc}]",
+              2 * n * 2 + (B * Cc + Cc) * 2,
+              lambda: (rnd(B, Cc, H, W), torch.empty((B, Cc, H, W), dtype=torch.bfloat16, device=dev)),
+              lambda x, z: hc.broadcast_binary(x, y_, bias, B, z=z))
+    if "activation_gelu_silu" in want:
+        entry("activation_gelu_silu", f"analog: bf16 [{R}, {K}], tanh-GELU", 2 * n * 2,
+              lambda: (rnd(R, K), torch.empty((R, K), dtype=torch.bfloat16, device=dev)),
+              lambda x, y: hc.activation_gelu_silu(x, "gelu", y=y))
+    if "reduce_sum_lastdim" in want:
+        entry("reduce_sum_lastdim", f"analog: bf16 [{R}, {K}] -> fp32 [{R}]", n * 2 + R * 4,
+              lambda: (rnd(R, K), torch.empty((R,), dtype=torch.float32, device=dev)),
+              lambda x, o: hc.reduce_sum_lastdim(x, out=o))
+    if "transpose_2d_4d" in want:
+        M = N = 8192
+        entry("transpose_2d_4d", f"analog: bf16 [{M}, {N}] -> [{N}, {M}]", 2 * M * N * 2,
+              lambda: (rnd(M, N), torch.empty((N, M), dtype=torch.bfloat16, device=dev)),
+              lambda x, o: hc.transpose_2d_4d(x, 0, out=o))
     return out
 
 

@@ -317,3 +317,15 @@ def test_layer_norm_outlier_first_element(cuda, hc_lib, oracle, kind, dim):
         assert_close(ref, host(y, oracle), 1e-4, 1e-4, f"outlier f32 dim {dim}")
     else:
         assert_close(ref, host(y, oracle), 1e-2, OUT_HALF_ULP[kind], f"outlier bf16 dim {dim}")
+
+
+@pytest.mark.parametrize("case", C.TRANSPOSE_4D_CASES + [(2, 64, 56, 56), (3, 5, 7, 9)],
+                         ids=lambda c: "{}x{}x{}x{}".format(*c))
+def test_transpose_4d_16bit_round_trip(cuda, hc_lib, oracle, case):
+    """2-byte elements take the 64x64-tile kernel (odd extents exercise its edge and misaligned-word paths)."""
+    n, c, h, w = case
+    xf = oracle.uniform(n * c * h * w, C.SEED).reshape(n, c, h, w)
+    x = dev(xf, "bf16", oracle)
+    y = hc_lib.transpose_2d_4d(x, 1)
+    assert np.array_equal(bits(y), oracle.transpose(bits(x), 1))
+    assert np.array_equal(bits(hc_lib.transpose_2d_4d(y, 2)), bits(x))
