@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extras]
 
-One step = one flash_attention_fwd_fused forward over the BASELINE configuration on every GPU:
+One step = one flash_attention_fwd_fused forward over the benchmarked configuration on every GPU:
 Q, K, V bf16 [B=16, H=32, S=8192, D=128], causal, scale 1/sqrt(128), O bf16 + lse fp32.
 Weak scaling: each rank owns a full 16x32-head shard of a global batch of 16*N (the work shards
 over batch x heads with no exchange, so there is no collective on the data path).  Time is
@@ -15,7 +15,7 @@ Extra keys of the JSON line:
                (hc_flash_attention_fwd_fused_host: pinned H2D copies, kernel, D2H copies, per step)
   cpu_baseline the reference golden (compiled from the reference sources into oracle/_ref) on the
                host cores, on a bounded sample (rank 0, N=1 only)
-  ops          the other BASELINE configurations (non-causal attention, matmul_bias, layer_norm,
+  ops          the other benchmarked configurations (non-causal attention, matmul_bias, layer_norm,
                rms_norm_rope_fused, elementwise_add) with their roofline fractions
   clocks       SM clocks and throttle reasons sampled with nvidia-smi during the timed region
 
@@ -394,7 +394,7 @@ def run_ours(args):
     del q, k, v, lse
     torch.cuda.empty_cache()
 
-    # ---------------- the other BASELINE configurations -----------------------------------------
+    # ---------------- the other benchmarked configurations ------------------------------------
     ops = {} if args.no_extras else run_extras(hc, d, dev, peaks, args)
 
     # ---------------- CPU baseline (rank 0, N=1) --------------------------------------------------
@@ -431,7 +431,7 @@ ANALOG_OPS = EXTRA_OPS[5:]
 
 
 def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
-    """The other BASELINE configurations, each timed alone (W=3, 20 launches)."""
+    """The other benchmarked configurations, each timed alone (W=3, 20 launches)."""
     import torch
 
     out = {}
@@ -621,7 +621,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--fa-batch", type=int, default=FA_B,
-                    help="attention batch per GPU (default 16, the BASELINE size; smaller only for profiling captures)")
+                    help="attention batch per GPU (default 16, the benchmarked size; smaller only for profiling captures)")
     ap.add_argument("--only", choices=EXTRA_OPS, default=None,
                     help="time one non-headline configuration alone and print its entry (profiling)")
     args = ap.parse_args()

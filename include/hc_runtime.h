@@ -38,7 +38,7 @@ typedef enum hc_status {
     HC_OK = 0,
     HC_ERR_INVALID = 1,      /* bad argument: null pointer, zero/unsupported size, bad enum */
     HC_ERR_CUDA = 2,         /* a CUDA runtime/driver call failed; see hc_last_error_string() */
-    HC_ERR_UNSUPPORTED = 3,  /* shape/dtype combination this build has no kernel for */
+    HC_ERR_UNSUPPORTED = 3,  /* shape/dtype combination this library has no kernel for */
     HC_ERR_TIMEOUT = 4,      /* a kernel's bounded wait expired (device error word was set) */
     HC_ERR_NO_DEVICE = 5,    /* no CUDA device visible */
     HC_ERR_INJECTED = 6      /* failure injected through HC_FAULT */

@@ -2,8 +2,8 @@
  * oracle.h -- CPU restatement of the reference harness's golden functions.
  *
  * TEST INFRASTRUCTURE ONLY.  Nothing in the product library links, loads or calls this code.
- * It is the checker for the CUDA kernels (tests/), the CPU baseline timed by bench.py, and the
- * reference for __graft_entry__.smoke().  Each function cites the golden it restates
+ * The CUDA kernels are compared against it (tests/), bench.py times it as the CPU baseline, and
+ * __graft_entry__.smoke() checks its one launch with it.  Each function cites the golden it restates
  * (paths are inside the z-zijie/ascend-npu-harness project).  Parity with the reference itself
  * is pinned by tests/test_oracle_pins.py against fixtures produced by the reference's own
  * golden sources (oracle/Makefile builds them into oracle/_ref/).

@@ -4,11 +4,11 @@ Golden: ops/flash_attention_fwd_fused/golden/flash_attention_fwd_fused_golden.cp
 fp64), restated in oracle/oracle.cpp with an added lse output.
   * the reference suite's 14 shape cases + its three hand-built tests, fp32 (SIMT kernel) at the
     reference tolerance 5e-4 and bf16 (tcgen05 kernel where D = D_v = 128) at max-abs 2e-2;
-  * the BASELINE subslice B=1 H=2 S=1024 D=128, N(0,1) inputs seeds 0/1/2, causal and non-causal,
+  * the check slice B=1 H=2 S=1024 D=128, N(0,1) inputs seeds 0/1/2, causal and non-causal,
     O max-abs 2e-2 and lse max-abs 2e-3;
   * ragged shapes for the tensor-core path (sequence tails, S_q != S_k, causal blocks that are not
     multiples of the 256-row work unit), fp16;
-  * the full BASELINE configuration B=16 H=32 S=8192 D=128 (causal and non-causal) against the
+  * the full benchmarked configuration B=16 H=32 S=8192 D=128 (causal and non-causal) against the
     independent fp32-math SIMT kernel on sampled heads, plus size-independent properties;
   * the host-buffer runner against the device entry point (bit-identical);
   * the bounded-wait machinery reporting an expired wait as HC_ERR_TIMEOUT.
@@ -24,7 +24,7 @@ from gpu_util import bits, dev, host, quantize
 
 pytestmark = pytest.mark.gpu
 
-O_TOL_BF16 = 2e-2   # BASELINE: max-abs 2e-2 vs the CPU golden
+O_TOL_BF16 = 2e-2   # max-abs 2e-2 vs the CPU golden (bf16 O)
 LSE_TOL = 2e-3
 
 
@@ -98,7 +98,7 @@ def test_reference_special_cases(cuda, hc_lib, oracle, kind):
 
 @pytest.mark.parametrize("causal", [0, 1], ids=["none", "causal"])
 def test_baseline_subslice(cuda, hc_lib, oracle, causal):
-    """BASELINE check slice: B=1 H=2 S=1024 D=128, Q/K/V ~ N(0,1) seeds 0/1/2, scale 1/sqrt(128)."""
+    """Check slice: B=1 H=2 S=1024 D=128, Q/K/V ~ N(0,1) seeds 0/1/2, scale 1/sqrt(128)."""
     B, H, S, D = 1, 2, 1024, 128
     q = oracle.normal(B * H * S * D, 0).reshape(B, H, S, D)
     k = oracle.normal(B * H * S * D, 1).reshape(B, H, S, D)
@@ -147,7 +147,7 @@ def test_large_logits_lazy_rescale(cuda, hc_lib, oracle):
 
 @pytest.mark.parametrize("causal", [1, 0], ids=["causal", "none"])
 def test_full_config_against_simt(cuda, hc_lib, oracle, causal):
-    """BASELINE: Q, K, V bf16 [16, 32, 8192, 128] ~ N(0,1) (device generator seeds 0/1/2).
+    """Benchmarked configuration: Q, K, V bf16 [16, 32, 8192, 128] ~ N(0,1) (device generator seeds 0/1/2).
     Sampled heads are recomputed by the fp32-math SIMT kernel (an independent code path pinned
     to the oracle by test_reference_cases_f32); every row is checked for the convex-combination
     property min_j V <= O <= max_j V and a finite lse."""

@@ -2,7 +2,7 @@
 
 fp32 (SIMT kernel): the reference's shape list at its tolerance 1e-4.  bf16/fp16 (tcgen05 kernel):
 rel-err <= 1e-2 against the fp32 golden on the quantised inputs, including tile tails, plus the
-BASELINE 8192^3 configuration checked on 128 sampled rows (both shard edges at 2/4/8 GPUs)."""
+benchmarked 8192^3 configuration checked on 128 sampled rows (both shard edges at 2/4/8 GPUs)."""
 from __future__ import annotations
 
 import numpy as np
@@ -48,7 +48,7 @@ def test_matmul_no_bias_and_identity(cuda, hc_lib, oracle):
 
 
 def test_matmul_config_sampled_rows(cuda, hc_lib, oracle):
-    """BASELINE: A, B bf16 [8192, 8192] ~ N(0,1)/sqrt(K), bias ~ N(0, 0.1); rel-err <= 1e-2 vs the
+    """Benchmarked configuration: A, B bf16 [8192, 8192] ~ N(0,1)/sqrt(K), bias ~ N(0, 0.1); rel-err <= 1e-2 vs the
     fp32 golden on 128 sampled rows (including rows 0, 1023/1024, 2047/2048, 4095/4096, 8191)."""
     M = K = N = 8192
     sk = np.float32(1.0 / np.sqrt(K))

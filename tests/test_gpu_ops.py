@@ -3,7 +3,7 @@
 For every case of the reference's GTest suites (tests/cases.py) the CUDA kernel, called through
 the C ABI, is compared with the oracle on the same inputs: bit-exact for elementwise add, axpy,
 broadcast and transposes (fp32 and 16-bit), and within the reference's tolerances otherwise
-(activation 1e-5, reduce 1e-4, layer_norm / rms_norm_rope 1e-4 in fp32).  The BASELINE
+(activation 1e-5, reduce 1e-4, layer_norm / rms_norm_rope 1e-4 in fp32).  The benchmarked
 configurations run at full size with their stated tolerances (layer_norm max-abs 1e-2,
 rms_norm_rope max-abs 2e-2, elementwise_add bit-exact); for 16-bit outputs an element also passes
 when it is within half an output ulp (relative) of the fp32 golden, because above |y| = 2.56
@@ -41,7 +41,7 @@ def test_elementwise_add(cuda, hc_lib, oracle, shape, kind):
 
 
 def test_elementwise_add_config_bit_exact(cuda, hc_lib, oracle):
-    """BASELINE config: fp16 [4096, 8192], x ~ U[-1,1] seed 0, y seed 1, bit-exact."""
+    """Benchmarked configuration: fp16 [4096, 8192], x ~ U[-1,1] seed 0, y seed 1, bit-exact."""
     n = 4096 * 8192
     x = oracle.uniform(n, 0).reshape(4096, 8192)
     y = oracle.uniform(n, 1).reshape(4096, 8192)
@@ -188,7 +188,7 @@ def test_layer_norm_constant_row(cuda, hc_lib, oracle):
 
 @pytest.mark.parametrize("kind", ["bf16", "f16"])
 def test_layer_norm_config(cuda, hc_lib, oracle, kind):
-    """BASELINE config: bf16 [16384, 4096], x ~ N(0,1) seed 0, gamma ~ U[0.5,1.5], beta ~ U[-0.1,0.1],
+    """Benchmarked configuration: bf16 [16384, 4096], x ~ N(0,1) seed 0, gamma ~ U[0.5,1.5], beta ~ U[-0.1,0.1],
     eps 1e-5, max-abs 1e-2 (checked on every row)."""
     rows, dim = 16384, 4096
     x = oracle.normal(rows * dim, 0).reshape(rows, dim)
@@ -228,7 +228,7 @@ def test_rms_norm_rope_heads_and_styles(cuda, hc_lib, oracle, style, H, rot):
 
 
 def test_rms_norm_rope_config(cuda, hc_lib, oracle):
-    """BASELINE config: x bf16 [8, 4096, 32, 128] ~ N(0,1) seed 0, weight ~ U[0.5,1.5], eps 1e-6,
+    """Benchmarked configuration: x bf16 [8, 4096, 32, 128] ~ N(0,1) seed 0, weight ~ U[0.5,1.5], eps 1e-6,
     rotate-half RoPE theta 10000, fp32 cos/sin; max-abs 2e-2 on every element."""
     B, S, Hh, D = 8, 4096, 32, 128
     x = oracle.normal(B * S * Hh * D, 0).reshape(B, S, Hh, D)
