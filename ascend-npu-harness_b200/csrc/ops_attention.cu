@@ -216,21 +216,29 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     }
 }
 
+// Descriptor bases are built once per call; each K-step adds its byte offset >> 4 to the low
+// word.  The MMAs are issued by one thread as a dependent chain, and a per-step rebuild of both
+// 64-bit descriptors made that chain long enough to leave the tensor pipe idle after each
+// softmax hand-off (4-5 % of the kernel's throughput on B200).
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr, uint32_t idesc) {
+    const Sw128Desc qd = make_sw128_desc2(q_addr, 16, 1024), kd = make_sw128_desc2(k_addr, 16, 1024);
 #pragma unroll
     for (uint32_t kk = 0; kk < kHD / 16; ++kk) {
-        uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-        mma_ss(d_tmem, make_sw128_desc(q_addr + off, 16, 1024), make_sw128_desc(k_addr + off, 16, 1024), idesc, kk > 0);
+        // K-step kk: 16 columns = 32 B inside a 128-B swizzle row; the second 64-column half
+        // of the head lives kHalfBytes further on.
+        const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+        mma_ss2(d_tmem, Sw128Desc{qd.lo + off, qd.hi}, Sw128Desc{kd.lo + off, kd.hi}, idesc, kk > 0);
     }
 }
 
 __device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, uint32_t idesc,
                                          bool accumulate) {
+    const Sw128Desc vd = make_sw128_desc2(v_addr, kHalfBytes, 1024);
 #pragma unroll
     for (uint32_t kk = 0; kk < kBN / 16; ++kk) {
         // 16 keys = 16 rows of the MN-major V panel = 2 swizzle atoms (2048 B); P: 8 columns.
-        mma_ts(o_tmem, p_tmem + kk * 8, make_sw128_desc(v_addr + kk * 2048, kHalfBytes, 1024), idesc,
-               (accumulate || kk > 0) ? 1u : 0u);
+        mma_ts2(o_tmem, p_tmem + kk * 8, Sw128Desc{vd.lo + kk * (2048 >> 4), vd.hi}, idesc,
+                (accumulate || kk > 0) ? 1u : 0u);
     }
 }
 

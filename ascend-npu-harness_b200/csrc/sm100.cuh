@@ -242,6 +242,40 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr, uint32_t
     return d;
 }
 
+// The same descriptor as two 32-bit words.  The start-address field (bits 0-13 of `lo`) holds
+// addr >> 4 < 2^14 for any shared-memory address, so adding (byte offset >> 4) to `lo` moves the
+// descriptor inside its tile without carrying into the leading-offset field.
+struct Sw128Desc {
+    uint32_t lo, hi;
+};
+__device__ __forceinline__ Sw128Desc make_sw128_desc2(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return Sw128Desc{((smem_addr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16),
+                     ((sbo_bytes >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29)};
+}
+
+// D(tmem) (+)= A(smem desc) * B(smem desc), descriptors given as words (see Sw128Desc).
+__device__ __forceinline__ void mma_ss2(uint32_t d_tmem, Sw128Desc a, Sw128Desc b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+        "mov.b64 da, {%1, %2};\n\tmov.b64 db, {%3, %4};\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d_tmem),
+        "r"(a.lo), "r"(a.hi), "r"(b.lo), "r"(b.hi), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D(tmem) (+)= A(tmem) * B(smem desc), the descriptor given as words.
+__device__ __forceinline__ void mma_ts2(uint32_t d_tmem, uint32_t a_tmem, Sw128Desc b, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+        "mov.b64 db, {%2, %3};\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "r"(b.lo), "r"(b.hi), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation.
 //   bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format (0 = f16, 1 = bf16),
 //   bit 15 A major (0 = K), bit 16 B major (0 = K, 1 = MN), bits 17-22 N >> 3, bits 24-28 M >> 4.
