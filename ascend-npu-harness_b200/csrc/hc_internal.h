@@ -29,6 +29,12 @@ bool fault_hit(const char* kind);
 // SM count of the current device (cached per device).
 int sm_count();
 
+// Blocks of `kernel` (launched with `threads` threads and `smem` bytes of dynamic shared memory)
+// that are resident on the whole current device at once, from the occupancy calculator (cached
+// per kernel, launch shape and device).  Grid-stride kernels use it as their grid cap: a larger
+// grid leaves its extra blocks a second, partly empty wave at the end of the launch.
+int resident_blocks(const void* kernel, int threads, size_t smem);
+
 // Size in bytes of one element of an hc_dtype, 0 for an unknown value.
 size_t dtype_size(int dtype);
 

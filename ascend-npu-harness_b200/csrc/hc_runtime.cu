@@ -81,6 +81,33 @@ bool fault_hit(const char* kind) {
     return n == g_fault_target;
 }
 
+int resident_blocks(const void* kernel, int threads, size_t smem) {
+    struct Entry {
+        const void* kernel;
+        int threads, dev;
+        size_t smem;
+        int blocks;
+    };
+    static std::mutex mu;
+    static std::vector<Entry> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const Entry& e : cache)
+            if (e.kernel == kernel && e.threads == threads && e.smem == smem && e.dev == dev) return e.blocks;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess || per_sm <= 0) {
+        cudaGetLastError();  // a failed query leaves its error pending; clear it
+        per_sm = 1;
+    }
+    const int blocks = per_sm * sm_count();
+    std::lock_guard<std::mutex> lock(mu);
+    cache.push_back(Entry{kernel, threads, dev, smem, blocks});
+    return blocks;
+}
+
 int sm_count() {
     static int cache[64] = {0};
     int dev = 0;

@@ -729,7 +729,7 @@ int launch_simt(const void* q, const void* k, const void* v, void* o, float* lse
                 const flash_attention_fwd_fused_tiling_data* t, cudaStream_t stream) {
     const uint64_t rows = static_cast<uint64_t>(t->B) * t->H * t->S_q;
     uint64_t blocks = (rows + 7) / 8;
-    uint64_t cap = static_cast<uint64_t>(sm_count()) * 8;
+    const uint64_t cap = static_cast<uint64_t>(resident_blocks(reinterpret_cast<const void*>(fa_fwd_simt_kernel<T>), 256, 0));
     if (blocks > cap) blocks = cap;
     fa_fwd_simt_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
         static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<T*>(o), lse,

@@ -920,7 +920,8 @@ int launch_rownorm(NormArgs a, void* stream) {
                                  static_cast<int>(smem)) != cudaSuccess)
             return cuda_fail(cudaGetLastError(), "cudaFuncSetAttribute(rownorm_scalar)");
     }
-    uint64_t cap = static_cast<uint64_t>(sm_count()) * 8;
+    const uint64_t cap =
+        static_cast<uint64_t>(resident_blocks(reinterpret_cast<const void*>(rownorm_scalar_kernel<T, KIND>), 256, smem));
     int blocks = static_cast<int>(a.rows < cap ? a.rows : cap);
     rownorm_scalar_kernel<T, KIND><<<blocks, 256, smem, s>>>(a);
     return check_launch(KIND == NormKind::kLayerNorm ? "layer_norm(scalar)" : "rms_norm_rope_fused(scalar)");
