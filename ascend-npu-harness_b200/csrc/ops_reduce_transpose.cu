@@ -7,8 +7,12 @@
 // modes are batched 2-D transposes staged through shared-memory tiles, bit-exact by construction.
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "hc_device.cuh"
 #include "hc_internal.h"
+#include "sm100.cuh"
+#include "tmap.h"
 
 namespace hc {
 namespace {
@@ -88,17 +92,17 @@ int launch_reduce(const void* x, float* out, uint32_t rows, uint32_t K, void* st
     const T* tx = static_cast<const T*>(x);
     bool vec = aligned16(x) && (K % elem<T>::kPack == 0);
     if (K <= 8192) {
+        auto kernel = vec ? reduce_rows_warp_kernel<T, true> : reduce_rows_warp_kernel<T, false>;
         int blocks = static_cast<int>((rows + 7) / 8);
-        int cap = sm_count() * 8;
+        const int cap = resident_blocks(reinterpret_cast<const void*>(kernel), 256, 0);
         if (blocks > cap) blocks = cap;
-        if (vec) reduce_rows_warp_kernel<T, true><<<blocks, 256, 0, s>>>(tx, out, rows, K);
-        else reduce_rows_warp_kernel<T, false><<<blocks, 256, 0, s>>>(tx, out, rows, K);
+        kernel<<<blocks, 256, 0, s>>>(tx, out, rows, K);
     } else {
+        auto kernel = vec ? reduce_rows_block_kernel<T, true> : reduce_rows_block_kernel<T, false>;
         int blocks = static_cast<int>(rows);
-        int cap = sm_count() * 8;
+        const int cap = resident_blocks(reinterpret_cast<const void*>(kernel), 256, 0);
         if (blocks > cap) blocks = cap;
-        if (vec) reduce_rows_block_kernel<T, true><<<blocks, 256, 0, s>>>(tx, out, rows, K);
-        else reduce_rows_block_kernel<T, false><<<blocks, 256, 0, s>>>(tx, out, rows, K);
+        kernel<<<blocks, 256, 0, s>>>(tx, out, rows, K);
     }
     return check_launch("reduce_sum_lastdim");
 }
@@ -109,22 +113,48 @@ int launch_reduce(const void* x, float* out, uint32_t rows, uint32_t K, void* st
 constexpr int kTile = 32;
 constexpr int kRowsPerPass = 8;
 
+// Tile index t -> (matrix b, first row r0, first column c0) with 32-bit multiply-shift divisions
+// (the launchers keep the tile count below 2^32); a 64-bit division per tile costs more
+// instructions than moving the tile.
+struct TileMap {
+    FastDiv per_batch, tiles_c;
+    uint32_t total;
+    size_t mat;
+    __device__ __forceinline__ void at(uint32_t t, uint32_t tile_r, uint32_t tile_c, uint64_t& b, uint32_t& r0,
+                                       uint32_t& c0) const {
+        const uint32_t bb = per_batch.div(t);
+        const uint32_t rem = t - bb * per_batch.d;
+        const uint32_t tr = tiles_c.div(rem);
+        b = bb;
+        r0 = tr * tile_r;
+        c0 = (rem - tr * tiles_c.d) * tile_c;
+    }
+};
+
+// Fills `m` for `batch` matrices of R x C in tiles of tile_r rows x tile_c columns; false when the
+// tile count does not fit 32 bits.
+bool make_tile_map(TileMap& m, uint32_t batch, uint32_t R, uint32_t C, uint32_t tile_r, uint32_t tile_c) {
+    const uint64_t tiles_r = (static_cast<uint64_t>(R) + tile_r - 1) / tile_r;
+    const uint64_t tiles_c = (static_cast<uint64_t>(C) + tile_c - 1) / tile_c;
+    const uint64_t total = tiles_r * tiles_c * batch;
+    if (tiles_r * tiles_c >= (1ull << 32) || total >= (1ull << 32)) return false;
+    m.per_batch.init(static_cast<uint32_t>(tiles_r * tiles_c));
+    m.tiles_c.init(static_cast<uint32_t>(tiles_c));
+    m.total = static_cast<uint32_t>(total);
+    m.mat = static_cast<size_t>(R) * C;
+    return true;
+}
+
 template <typename E>
 __global__ void __launch_bounds__(kTile * kRowsPerPass) transpose_kernel(const E* __restrict__ in, E* __restrict__ out,
-                                                                         uint32_t batch, uint32_t R, uint32_t C) {
+                                                                         uint32_t R, uint32_t C, TileMap map) {
     __shared__ E tile[kTile][kTile + 1];
-    const uint64_t tiles_r = (R + kTile - 1) / kTile;
-    const uint64_t tiles_c = (C + kTile - 1) / kTile;
-    const uint64_t per_batch = tiles_r * tiles_c;
-    const uint64_t total = per_batch * batch;
-    const size_t mat = static_cast<size_t>(R) * C;
-    for (uint64_t t = blockIdx.x; t < total; t += gridDim.x) {
-        uint64_t b = t / per_batch;
-        uint64_t rem = t % per_batch;
-        uint32_t r0 = static_cast<uint32_t>(rem / tiles_c) * kTile;
-        uint32_t c0 = static_cast<uint32_t>(rem % tiles_c) * kTile;
-        const E* src = in + b * mat;
-        E* dst = out + b * mat;
+    for (uint32_t t = blockIdx.x; t < map.total; t += gridDim.x) {
+        uint64_t b;
+        uint32_t r0, c0;
+        map.at(t, kTile, kTile, b, r0, c0);
+        const E* src = in + b * map.mat;
+        E* dst = out + b * map.mat;
         // Read rows r0.. of the tile (coalesced along c).
         for (int i = threadIdx.y; i < kTile; i += kRowsPerPass) {
             uint32_t r = r0 + i, c = c0 + threadIdx.x;
@@ -140,108 +170,270 @@ __global__ void __launch_bounds__(kTile * kRowsPerPass) transpose_kernel(const E
     }
 }
 
-// 2-byte elements: 64 x 64 tiles, so that every warp access is one 128-byte row segment (a 32 x 32
-// tile of 2-byte elements would move 64-byte segments).  A lane moves two neighbouring elements
-// as one 32-bit word (two 16-bit accesses where a word would be misaligned or cross the edge).
-// Shared-memory rows are 65 elements long: the transposed reads (rows 2l and 2l+1 of one column)
-// then fall on 32 different banks.
+// 2-byte elements: 64 x 64 tiles moved as 2 x 2 blocks.  On the way in, lane x of row-pair p
+// loads the 32-bit words (r, c..c+1) and (r+1, c..c+1), r = r0 + 2p, c = c0 + 2x; two byte
+// permutes turn them into the output words (c, r..r+1) and (c+1, r..r+1), which go to shared
+// memory as blk[h][x][p].  On the way out, lane x writes output word (c0 + 2q + h, r0 + 2x) from
+// blk[h][q][x].  Every warp access is a 128-byte row segment, and with rows of 33 words both
+// shared-memory phases touch 32 different banks.  Words that would be misaligned, or that cross
+// the matrix edge, are moved as two 16-bit accesses.
 constexpr int kT16 = 64;
 
 __global__ void __launch_bounds__(kTile * kRowsPerPass) transpose16_kernel(const uint16_t* __restrict__ in,
-                                                                           uint16_t* __restrict__ out, uint32_t batch,
-                                                                           uint32_t R, uint32_t C) {
-    constexpr int kRowsPerThread = kT16 / kRowsPerPass;  // 8
-    __shared__ uint16_t tile[kT16][kT16 + 1];
-    const uint64_t tiles_r = (R + kT16 - 1) / kT16;
-    const uint64_t tiles_c = (C + kT16 - 1) / kT16;
-    const uint64_t per_batch = tiles_r * tiles_c;
-    const uint64_t total = per_batch * batch;
-    const size_t mat = static_cast<size_t>(R) * C;
-    const uint32_t l2 = 2 * threadIdx.x;
-    // The tile's rows r0+i (i = threadIdx.y + 8k) are fetched into registers one tile ahead, so
-    // the loads of tile t+1 are in flight while tile t is written out.
-    struct Coord {
-        uint64_t b;
-        uint32_t r0, c0;
-    };
-    auto coord = [&](uint64_t t) {
-        const uint64_t rem = t % per_batch;
-        return Coord{t / per_batch, static_cast<uint32_t>(rem / tiles_c) * kT16, static_cast<uint32_t>(rem % tiles_c) * kT16};
-    };
+                                                                           uint16_t* __restrict__ out, uint32_t R,
+                                                                           uint32_t C, TileMap map) {
+    constexpr int kPairsPerThread = kT16 / 2 / kRowsPerPass;  // 4 row pairs = 8 loaded words
+    constexpr int kOutPerThread = kT16 / kRowsPerPass;         // 8 output words
+    __shared__ uint32_t blk[2][kT16 / 2][kT16 / 2 + 1];
+    const uint32_t lx = threadIdx.x, ly = threadIdx.y;
     // A 32-bit access needs an even element offset from the 4-byte aligned buffer start: the
     // parity is that of the batch base b * mat plus the offset inside the matrix.
-    auto fetch = [&](const Coord& k, uint32_t (&w)[kRowsPerThread]) {
-        const uint16_t* src = in + k.b * mat;
-        const size_t base_par = (k.b * mat) & 1;
-#pragma unroll
-        for (int q = 0; q < kRowsPerThread; ++q) {
-            const uint32_t r = k.r0 + threadIdx.y + q * kRowsPerPass, c = k.c0 + l2;
-            uint32_t v = 0;
-            if (r < R) {
-                const size_t o = static_cast<size_t>(r) * C + c;
-                if (c + 1 < C && ((base_par + o) & 1) == 0) {
-                    v = __ldcs(reinterpret_cast<const unsigned int*>(src + o));
-                } else {
-                    if (c < C) v = src[o];
-                    if (c + 1 < C) v |= static_cast<uint32_t>(src[o + 1]) << 16;
-                }
+    auto load_word = [&](const uint16_t* src, size_t base_par, uint32_t r, uint32_t c) -> uint32_t {
+        uint32_t v = 0;
+        if (r < R) {
+            const size_t o = static_cast<size_t>(r) * C + c;
+            if (c + 1 < C && ((base_par + o) & 1) == 0) {
+                v = __ldcs(reinterpret_cast<const unsigned int*>(src + o));
+            } else {
+                if (c < C) v = src[o];
+                if (c + 1 < C) v |= static_cast<uint32_t>(src[o + 1]) << 16;
             }
-            w[q] = v;
+        }
+        return v;
+    };
+    // The words of tile t+1 are loaded into registers while tile t is written out.
+    auto fetch = [&](uint32_t t, uint32_t (&w)[2 * kPairsPerThread]) {
+        uint64_t b;
+        uint32_t r0, c0;
+        map.at(t, kT16, kT16, b, r0, c0);
+        const uint16_t* src = in + b * map.mat;
+        const size_t base_par = (b * map.mat) & 1;
+#pragma unroll
+        for (int k = 0; k < kPairsPerThread; ++k) {
+            const uint32_t r = r0 + 2 * (ly + k * kRowsPerPass), c = c0 + 2 * lx;
+            w[2 * k] = load_word(src, base_par, r, c);
+            w[2 * k + 1] = load_word(src, base_par, r + 1, c);
         }
     };
-    uint32_t w[kRowsPerThread];
-    uint64_t t = blockIdx.x;
-    if (t < total) fetch(coord(t), w);
-    for (; t < total; t += gridDim.x) {
-        const Coord k = coord(t);
+    uint32_t w[2 * kPairsPerThread];
+    uint32_t t = blockIdx.x;
+    if (t < map.total) fetch(t, w);
+    for (; t < map.total; t += gridDim.x) {
 #pragma unroll
-        for (int q = 0; q < kRowsPerThread; ++q) {
-            const int i = threadIdx.y + q * kRowsPerPass;
-            tile[i][l2] = static_cast<uint16_t>(w[q]);
-            tile[i][l2 + 1] = static_cast<uint16_t>(w[q] >> 16);
+        for (int k = 0; k < kPairsPerThread; ++k) {
+            const int p = ly + k * kRowsPerPass;
+            blk[0][lx][p] = __byte_perm(w[2 * k], w[2 * k + 1], 0x5410);  // low halves: column c
+            blk[1][lx][p] = __byte_perm(w[2 * k], w[2 * k + 1], 0x7632);  // high halves: column c + 1
         }
         __syncthreads();
-        if (t + gridDim.x < total) fetch(coord(t + gridDim.x), w);
-        // Rows c0.. of the output, two elements per lane.
-        uint16_t* dst = out + k.b * mat;
-        const size_t base_par = (k.b * mat) & 1;
+        if (t + gridDim.x < map.total) fetch(t + gridDim.x, w);
+        uint64_t b;
+        uint32_t r0, c0;
+        map.at(t, kT16, kT16, b, r0, c0);
+        uint16_t* dst = out + b * map.mat;
+        const size_t base_par = (b * map.mat) & 1;
+        const uint32_t r = r0 + 2 * lx;
 #pragma unroll
-        for (int q = 0; q < kRowsPerThread; ++q) {
-            const int i = threadIdx.y + q * kRowsPerPass;
-            const uint32_t c = k.c0 + i, r = k.r0 + l2;
+        for (int q = 0; q < kOutPerThread; ++q) {
+            const int idx = ly + q * kRowsPerPass;  // 0..63: column pair idx >> 1, half idx & 1
+            const int h = idx & 1, cp = idx >> 1;
+            const uint32_t c = c0 + 2 * cp + h;
             if (c >= C) continue;
+            const uint32_t v = blk[h][cp][lx];
             const size_t o = static_cast<size_t>(c) * R + r;
-            const uint16_t lo = tile[l2][i], hi = tile[l2 + 1][i];
             if (r + 1 < R && ((base_par + o) & 1) == 0) {
-                __stcs(reinterpret_cast<unsigned int*>(dst + o),
-                       static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16));
+                __stcs(reinterpret_cast<unsigned int*>(dst + o), v);
             } else {
-                if (r < R) dst[o] = lo;
-                if (r + 1 < R) dst[o + 1] = hi;
+                if (r < R) dst[o] = static_cast<uint16_t>(v);
+                if (r + 1 < R) dst[o + 1] = static_cast<uint16_t>(v >> 16);
             }
         }
         __syncthreads();
     }
 }
 
-int launch_transpose16(const void* src, void* dst, uint32_t batch, uint32_t R, uint32_t C, void* stream) {
-    const uint64_t tiles = static_cast<uint64_t>((R + kT16 - 1) / kT16) * ((C + kT16 - 1) / kT16) * batch;
-    const uint64_t cap = static_cast<uint64_t>(sm_count()) * 8;
-    const int blocks = static_cast<int>(tiles < cap ? tiles : cap);
+template <typename E>
+int launch_transpose(const void* src, void* dst, uint32_t batch, uint32_t R, uint32_t C, void* stream) {
+    TileMap map;
+    if (!make_tile_map(map, batch, R, C, kTile, kTile))
+        return fail(HC_ERR_INVALID, "transpose_2d_4d: %u matrices of %u x %u exceed 2^32 tiles", batch, R, C);
+    const uint64_t cap = static_cast<uint64_t>(
+        resident_blocks(reinterpret_cast<const void*>(transpose_kernel<E>), kTile * kRowsPerPass, 0));
+    const int blocks = static_cast<int>(map.total < cap ? map.total : cap);
     if (blocks == 0) return ok();
-    transpose16_kernel<<<blocks, dim3(kTile, kRowsPerPass), 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), batch, R, C);
+    transpose_kernel<E><<<blocks, dim3(kTile, kRowsPerPass), 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const E*>(src), static_cast<E*>(dst), R, C, map);
     return check_launch("transpose_2d_4d");
 }
 
-template <typename E>
-int launch_transpose(const void* src, void* dst, uint32_t batch, uint32_t R, uint32_t C, void* stream) {
-    uint64_t tiles = static_cast<uint64_t>((R + kTile - 1) / kTile) * ((C + kTile - 1) / kTile) * batch;
-    uint64_t cap = static_cast<uint64_t>(sm_count()) * 8;
-    int blocks = static_cast<int>(tiles < cap ? tiles : cap);
+// 2-byte elements with R and C multiples of 8 and 16-byte aligned buffers: tiles of 256 rows x 64
+// columns arrive by TMA (128-byte swizzle) in a 3-stage ring, so up to three 32 KB tiles per block
+// are in flight while one is written out.  Warp w owns tile rows 64 (w >> 1) .. +63 and 16-byte
+// column chunks 4 (w & 1) .. +3.  Its lane (rb, jj) reads chunk j = 4 (w & 1) + jj of the eight rows
+// row0 + i, row0 = 64 (w >> 1) + 8 rb (the 128-byte swizzle puts it in slot j ^ i), transposes that
+// 8 x 8 block in registers (one byte permute per output word) and writes eight 16-byte words:
+// output rows c0 + 8j + m, columns r0 + row0 .. +7.  The eight lanes with the same jj write one
+// whole 128-byte line of an output row; a read costs eight wavefronts (four distinct slots per
+// row), which shared memory absorbs easily at this traffic.
+using namespace sm100;
+
+constexpr uint32_t kTmaRows = 256, kTmaCols = 64, kTmaStages = 3, kTmaThreads = 256;
+constexpr uint32_t kTmaTileBytes = kTmaRows * kTmaCols * 2;
+constexpr size_t kTmaSmemBytes = kTmaStages * kTmaTileBytes + 1024;  // + alignment slack
+constexpr uint32_t kErrTransposeWait = 1u, kErrTransposeDrain = 2u;
+static_assert(kTmaRows == 64 * (kTmaThreads / 32 / 2) && kTmaCols == 64, "warp pairs cover 64 rows x 64 columns");
+
+__device__ uint32_t g_transpose_error_word;
+
+__global__ void __launch_bounds__(kTmaThreads) transpose16_tma_kernel(const __grid_constant__ CUtensorMap tm_in,
+                                                                      uint16_t* __restrict__ out, uint32_t R,
+                                                                      uint32_t C, TileMap map) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full[kTmaStages];
+    __shared__ uint32_t abort_flag;
+    const uint32_t tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+    if (tid == 0) {
+        abort_flag = 0;
+        for (uint32_t s = 0; s < kTmaStages; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+        prefetch_tmap(&tm_in);
+    }
+    __syncthreads();
+    auto issue = [&](uint32_t t, uint32_t s) {
+        uint64_t b;
+        uint32_t r0, c0;
+        map.at(t, kTmaRows, kTmaCols, b, r0, c0);
+        mbar_arrive_expect_tx(&full[s], kTmaTileBytes);  // a box counts in full, zero-filled edges included
+        tma_load_3d(smem + s * kTmaTileBytes, &tm_in, &full[s], static_cast<int32_t>(c0), static_cast<int32_t>(r0),
+                    static_cast<int32_t>(b));
+    };
+    const uint64_t grid = gridDim.x;
+    uint32_t issued = 0;  // tiles issued by thread 0 (only thread 0's count is used)
+    if (tid == 0)
+        for (uint32_t s = 0; s < kTmaStages && blockIdx.x + s * grid < map.total; ++s, ++issued)
+            issue(static_cast<uint32_t>(blockIdx.x + s * grid), s);
+    // warp w: tile rows 64 (w >> 1) .. +63, column chunks 4 (w & 1) .. +3; lane (rb, jj): 8 x 4
+    const uint32_t rb = lane >> 2, j = 4 * (warp & 1) + (lane & 3);
+    const uint32_t row0 = 64 * (warp >> 1) + rb * 8;  // first of this lane's eight tile rows (a multiple of 8)
+    uint32_t k = 0;
+    for (uint64_t t = blockIdx.x; t < map.total; t += grid, ++k) {
+        const uint32_t s = k % kTmaStages;
+        const bool ok = mbar_wait_bounded(&full[s], (k / kTmaStages) & 1u, &abort_flag, &g_transpose_error_word,
+                                          kErrTransposeWait);
+        if (ok) {
+            uint64_t b;
+            uint32_t r0, c0;
+            map.at(static_cast<uint32_t>(t), kTmaRows, kTmaCols, b, r0, c0);
+            const uint8_t* st = smem + s * kTmaTileBytes;
+            uint32_t a[8][4];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                // row0 + i has (row & 7) == i: its chunk j sits in slot j ^ i
+                const uint4 v = *reinterpret_cast<const uint4*>(st + (row0 + i) * 128 + ((j ^ i) << 4));
+                a[i][0] = v.x;
+                a[i][1] = v.y;
+                a[i][2] = v.z;
+                a[i][3] = v.w;
+            }
+            const uint32_t r = r0 + row0;
+            if (r < R) {  // R % 8 == 0: the lane's eight rows are all inside or all outside
+                uint16_t* dst = out + b * map.mat + r;
+#pragma unroll
+                for (int m = 0; m < 8; ++m) {
+                    const uint32_t c = c0 + 8 * j + m;
+                    if (c >= C) continue;
+                    const uint32_t sel = (m & 1) ? 0x7632u : 0x5410u;  // high or low halves
+                    const int w = m >> 1;
+                    uint4 o;
+                    o.x = __byte_perm(a[0][w], a[1][w], sel);
+                    o.y = __byte_perm(a[2][w], a[3][w], sel);
+                    o.z = __byte_perm(a[4][w], a[5][w], sel);
+                    o.w = __byte_perm(a[6][w], a[7][w], sel);
+                    __stcs(reinterpret_cast<uint4*>(dst + static_cast<size_t>(c) * R), o);
+                }
+            }
+        }
+        // Every thread is done with stage s (or one of them gave up: then all leave together).
+        if (!__syncthreads_and(ok)) break;
+        if (tid == 0) {
+            const uint64_t tn = t + kTmaStages * grid;
+            if (tn < map.total) {
+                issue(static_cast<uint32_t>(tn), s);
+                ++issued;
+            }
+        }
+    }
+    // After a timeout, wait (bounded) for the copies still in flight before the block's shared
+    // memory is released.
+    if (tid == 0) {
+        volatile uint32_t never = 0;
+        for (uint32_t q = k; q < issued; ++q)
+            mbar_wait_bounded(&full[q % kTmaStages], (q / kTmaStages) & 1u, &never, &g_transpose_error_word,
+                              kErrTransposeDrain, 1000000000ull);
+    }
+}
+
+uint32_t read_transpose_error_word(const char** name) {
+    *name = "transpose_2d_4d";
+    uint32_t word = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&word, g_transpose_error_word, sizeof(word)) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (word) cudaMemcpyToSymbol(g_transpose_error_word, &zero, sizeof(zero));
+    return word;
+}
+
+// Returns false when the TMA path does not apply (the caller then takes transpose16_kernel);
+// otherwise launches it and sets *status.
+bool launch_transpose16_tma(const void* src, void* dst, uint32_t batch, uint32_t R, uint32_t C, void* stream,
+                            int* status) {
+    if ((reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15) || (R & 7) || (C & 7))
+        return false;
+    TileMap map;
+    if (!make_tile_map(map, batch, R, C, kTmaRows, kTmaCols)) return false;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        register_error_word(read_transpose_error_word);
+        attr_err = cudaFuncSetAttribute(transpose16_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(kTmaSmemBytes));
+    });
+    if (attr_err != cudaSuccess) {
+        *status = cuda_fail(attr_err, "cudaFuncSetAttribute(transpose16_tma_kernel)");
+        return true;
+    }
+    CUtensorMap tm;
+    const uint64_t dims[3] = {C, R, batch};
+    const uint64_t strides[2] = {static_cast<uint64_t>(C) * 2, static_cast<uint64_t>(R) * C * 2};
+    const uint32_t box[3] = {kTmaCols, kTmaRows, 1};
+    *status = encode_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, src, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (*status != HC_OK) return true;
+    const uint64_t cap = static_cast<uint64_t>(
+        resident_blocks(reinterpret_cast<const void*>(transpose16_tma_kernel), kTmaThreads, kTmaSmemBytes));
+    const int blocks = static_cast<int>(map.total < cap ? map.total : cap);
+    if (blocks == 0) {
+        *status = ok();
+        return true;
+    }
+    transpose16_tma_kernel<<<blocks, kTmaThreads, kTmaSmemBytes, static_cast<cudaStream_t>(stream)>>>(
+        tm, static_cast<uint16_t*>(dst), R, C, map);
+    *status = check_launch("transpose_2d_4d(tma)");
+    return true;
+}
+
+int launch_transpose16(const void* src, void* dst, uint32_t batch, uint32_t R, uint32_t C, void* stream) {
+    int status = HC_OK;
+    if (launch_transpose16_tma(src, dst, batch, R, C, stream, &status)) return status;
+    TileMap map;
+    if (!make_tile_map(map, batch, R, C, kT16, kT16)) return launch_transpose<uint16_t>(src, dst, batch, R, C, stream);
+    const uint64_t cap = static_cast<uint64_t>(
+        resident_blocks(reinterpret_cast<const void*>(transpose16_kernel), kTile * kRowsPerPass, 0));
+    const int blocks = static_cast<int>(map.total < cap ? map.total : cap);
     if (blocks == 0) return ok();
-    transpose_kernel<E><<<blocks, dim3(kTile, kRowsPerPass), 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const E*>(src), static_cast<E*>(dst), batch, R, C);
+    transpose16_kernel<<<blocks, dim3(kTile, kRowsPerPass), 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), R, C, map);
     return check_launch("transpose_2d_4d");
 }
 

@@ -322,7 +322,39 @@ def test_layer_norm_outlier_first_element(cuda, hc_lib, oracle, kind, dim):
 @pytest.mark.parametrize("case", C.TRANSPOSE_4D_CASES + [(2, 64, 56, 56), (3, 5, 7, 9)],
                          ids=lambda c: "{}x{}x{}x{}".format(*c))
 def test_transpose_4d_16bit_round_trip(cuda, hc_lib, oracle, case):
-    """2-byte elements take the 64x64-tile kernel (odd extents exercise its edge and misaligned-word paths)."""
+    """2-byte elements: extents that are not multiples of 8 take the 64x64 register-tile kernel (odd extents
+    exercise its edge and misaligned-word paths); the others take the TMA-fed kernel."""
+    n, c, h, w = case
+    xf = oracle.uniform(n * c * h * w, C.SEED).reshape(n, c, h, w)
+    x = dev(xf, "bf16", oracle)
+    y = hc_lib.transpose_2d_4d(x, 1)
+    assert np.array_equal(bits(y), oracle.transpose(bits(x), 1))
+    assert np.array_equal(bits(hc_lib.transpose_2d_4d(y, 2)), bits(x))
+
+
+@pytest.mark.parametrize("case", [(8, 8), (264, 72), (520, 200), (1024, 4096), (4104, 8), (8, 4104)],
+                         ids=lambda c: "{}x{}".format(*c))
+def test_transpose_16bit_tma_tiles(cuda, hc_lib, oracle, case):
+    """Extents that are multiples of 8 take the TMA-fed kernel (256 x 64 tiles): partial tiles at both
+    edges, and more tiles than resident blocks.  An offset view (not 16-byte aligned) of the same
+    data takes the register-tile kernel and must give the same bits."""
+    import torch
+
+    M, N = case
+    xi = torch.from_numpy((np.arange(M * N, dtype=np.int64) % 65521).astype(np.int16).reshape(M, N)).cuda()
+    want = xi.cpu().t().contiguous()
+    y = hc_lib.transpose_2d_4d(xi.view(torch.bfloat16), 0)
+    assert torch.equal(y.view(torch.int16).cpu(), want)
+    # two elements in: 4-byte aligned (register-tile kernel), not 16-byte aligned (no TMA)
+    buf = torch.empty(M * N + 2, dtype=torch.int16, device="cuda")
+    buf[2:].copy_(xi.reshape(-1))
+    xo = buf[2:].view(M, N).view(torch.bfloat16)
+    assert torch.equal(hc_lib.transpose_2d_4d(xo, 0).view(torch.int16).cpu(), want)
+
+
+@pytest.mark.parametrize("case", [(3, 24, 17, 8), (2, 8, 64, 48)], ids=lambda c: "{}x{}x{}x{}".format(*c))
+def test_transpose_4d_16bit_tma_round_trip(cuda, hc_lib, oracle, case):
+    """Batched NCHW <-> NHWC with channel and plane sizes that are multiples of 8 (TMA-fed kernel)."""
     n, c, h, w = case
     xf = oracle.uniform(n * c * h * w, C.SEED).reshape(n, c, h, w)
     x = dev(xf, "bf16", oracle)
