@@ -66,6 +66,8 @@ PROFILE_FILES = {
     "layer_norm": "layer_norm_16384x4096_bf16",
     "rms_norm_rope_fused": "rms_norm_rope_fused_8x4096x32x128_bf16",
     "elementwise_add": "elementwise_add_4096x8192_f16",
+    "activation_gelu_silu": "activation_gelu_silu_16384x4096_bf16",
+    "transpose_2d_4d": "transpose_2d_4d_8192x8192_bf16",
 }
 
 
@@ -562,7 +564,7 @@ def run_analogs(hc, d: Dist, dev, peaks, want, steps, warm, alternate) -> dict:
         out[name] = {"value": d.world * gbs, "unit": "GB/s", "per_gpu": gbs, "ms": ms, "config": config,
                      "timing": f"{steps} back-to-back launches alternating two buffer sets, no L2 flush",
                      "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                                  "algorithmic_bytes_per_launch": bytes_, "traffic": None}}
+                                  "algorithmic_bytes_per_launch": bytes_, "traffic": profile_traffic(name)}}
 
     n = R * K
     if "axpy_scalar_affine" in want:
