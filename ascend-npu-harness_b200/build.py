@@ -105,6 +105,32 @@ def build_host(force: bool = False, verbose: bool = False) -> Path:
     return HOST_TARGET
 
 
+TORCH_TARGET = LIB / "libhc_torch.so"
+
+
+def build_torch(force: bool = False, verbose: bool = False) -> Path:
+    """Compiles csrc/torch_ops.cpp (the `hc` torch custom-op library over the C ABI) into lib/libhc_torch.so,
+    linked to libhc_b200.so.  Load it with torch.ops.load_library()."""
+    src = CSRC / "torch_ops.cpp"
+    deps = [src, TARGET] + sorted(INCLUDE.glob("*.h"))
+    if not force and not _stale(TORCH_TARGET, deps):
+        return TORCH_TARGET
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    cxx = shutil.which("g++") or "g++"
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           *[f"-I{p}" for p in ce.include_paths(device_type="cuda")], f"-I{INCLUDE}", str(src), "-o", str(TORCH_TARGET),
+           *[f"-L{p}" for p in ce.library_paths(device_type="cuda")], "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+           "-ltorch_cuda", f"-L{LIB}", "-lhc_b200", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch op library build failed:\n{r.stderr[-6000:]}")
+    return TORCH_TARGET
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -112,6 +138,7 @@ if __name__ == "__main__":
     a = ap.parse_args()
     try:
         print(build(a.force, a.verbose))
+        print(build_torch(a.force, a.verbose))
     except RuntimeError as e:
         print(e, file=sys.stderr)
         sys.exit(1)

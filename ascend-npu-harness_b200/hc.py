@@ -19,6 +19,7 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "lib" / "libhc_b200.so"
+TORCH_OPS_PATH = HERE / "lib" / "libhc_torch.so"
 
 HC_OK, HC_ERR_INVALID, HC_ERR_CUDA, HC_ERR_UNSUPPORTED, HC_ERR_TIMEOUT, HC_ERR_NO_DEVICE, HC_ERR_INJECTED = range(7)
 DT_F32, DT_F16, DT_BF16, DT_I32, DT_I8, DT_U8 = range(6)
@@ -324,6 +325,22 @@ def flash_attention_fwd(q, k, v, causal: bool, scale: float | None = None, with_
                                                      _ptr(lse) if with_lse else None, C.byref(t), dtype_code(q),
                                                      _stream(stream)))
     return out, (lse if with_lse else None)
+
+
+_torch_ops_loaded = False
+
+
+def load_torch_ops():
+    """Registers the `hc` torch custom ops (lib/libhc_torch.so, csrc/torch_ops.cpp) and returns torch.ops.hc.
+    The ops call the same C ABI as this module, on the current CUDA stream; they raise on CPU tensors."""
+    global _torch_ops_loaded
+    torch = _torch()
+    if not _torch_ops_loaded:
+        if not TORCH_OPS_PATH.exists():
+            raise HcError(HC_ERR_INVALID, f"{TORCH_OPS_PATH} is missing; run ascend-npu-harness_b200/build.py")
+        torch.ops.load_library(str(TORCH_OPS_PATH))
+        _torch_ops_loaded = True
+    return torch.ops.hc
 
 
 def check_device_error() -> None:
