@@ -75,6 +75,7 @@ struct Params {
     void* o;
     float* lse;
     uint32_t S_q, S_k, BH, n_qblk, num_pairs;  // num_pairs = BH * ceil(n_qblk / 2)
+    uint32_t group;    // query heads per K/V head: K/V head of flattened query head bh is bh / group
     float scale_log2;  // softmax scale * log2(e), > 0
     uint32_t causal;
 };
@@ -324,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (uint32_t h = 0; h < 2; ++h)
                             tma_load_3d(smem + kOffKV + stage * kTileBytes + h * kHalfBytes, kv ? &tm_v : &tm_k,
                                         &bars->kv_full[stage], static_cast<int32_t>(h * 64),
-                                        static_cast<int32_t>(j * kBN), static_cast<int32_t>(bh));
+                                        static_cast<int32_t>(j * kBN), static_cast<int32_t>(bh / p.group));
                         pend_valid |= 1u << stage;
                         pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
                         if (++stage == kStages) {
@@ -586,7 +587,7 @@ __global__ void __launch_bounds__(256) fa_fwd_simt_kernel(const T* __restrict__ 
                                                           const T* __restrict__ v, T* __restrict__ o,
                                                           float* __restrict__ lse, uint32_t BH, uint32_t S_q,
                                                           uint32_t S_k, uint32_t D, uint32_t Dv, float scale,
-                                                          uint32_t causal) {
+                                                          uint32_t causal, uint32_t group) {
     constexpr int kMaxD = 256;
     __shared__ float qs[8][kMaxD];
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -607,7 +608,7 @@ __global__ void __launch_bounds__(256) fa_fwd_simt_kernel(const T* __restrict__ 
             const uint32_t kj = k0 + lane;
             float sc = -INFINITY;
             if (kj < kend) {
-                const T* krow = k + (bh * S_k + kj) * D;
+                const T* krow = k + (bh / group * S_k + kj) * D;
                 float dot = 0.f;
                 for (uint32_t d = 0; d < D; ++d) dot = fmaf(qs[warp][d], elem<T>::to_f(krow[d]), dot);
                 sc = dot * scale;
@@ -625,7 +626,7 @@ __global__ void __launch_bounds__(256) fa_fwd_simt_kernel(const T* __restrict__ 
             const uint32_t cnt = min(32u, kend - k0);
             for (uint32_t jj = 0; jj < cnt; ++jj) {
                 const float pv = __shfl_sync(0xffffffffu, pj, jj);
-                const T* vrow = v + (bh * S_k + k0 + jj) * Dv;
+                const T* vrow = v + (bh / group * S_k + k0 + jj) * Dv;
 #pragma unroll
                 for (int i = 0; i < kMaxD / 32; ++i) {
                     uint32_t d = lane + 32 * i;
@@ -677,7 +678,7 @@ thread_local int t_last_path = 0;
 
 template <bool kBF16>
 int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
-              const flash_attention_fwd_fused_tiling_data* t, cudaStream_t stream) {
+              const flash_attention_fwd_fused_tiling_data* t, uint32_t kv_heads, cudaStream_t stream) {
     static std::once_flag reg_once;
     std::call_once(reg_once, [] { register_error_word(read_error_word); });
     const uint64_t BH = static_cast<uint64_t>(t->B) * t->H;
@@ -691,7 +692,7 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
         if (rc) return rc;
     }
     {
-        uint64_t dims[3] = {kHD, t->S_k, BH};
+        uint64_t dims[3] = {kHD, t->S_k, static_cast<uint64_t>(t->B) * kv_heads};
         uint64_t strides[2] = {kHD * 2, static_cast<uint64_t>(t->S_k) * kHD * 2};
         int rc = encode_tmap(&tmk, dt, 3, k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
@@ -704,6 +705,7 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
     prm.S_q = t->S_q;
     prm.S_k = t->S_k;
     prm.BH = static_cast<uint32_t>(BH);
+    prm.group = t->H / kv_heads;
     prm.n_qblk = (t->S_q + 2 * kBM - 1) / (2 * kBM);
     const uint64_t pairs = BH * ((prm.n_qblk + 1) / 2);
     if (BH * prm.n_qblk > 0xffffffffull) return fail(HC_ERR_UNSUPPORTED, "flash_attention: too many work units");
@@ -726,14 +728,14 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
 
 template <typename T>
 int launch_simt(const void* q, const void* k, const void* v, void* o, float* lse,
-                const flash_attention_fwd_fused_tiling_data* t, cudaStream_t stream) {
+                const flash_attention_fwd_fused_tiling_data* t, uint32_t kv_heads, cudaStream_t stream) {
     const uint64_t rows = static_cast<uint64_t>(t->B) * t->H * t->S_q;
     uint64_t blocks = (rows + 7) / 8;
     const uint64_t cap = static_cast<uint64_t>(resident_blocks(reinterpret_cast<const void*>(fa_fwd_simt_kernel<T>), 256, 0));
     if (blocks > cap) blocks = cap;
     fa_fwd_simt_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
         static_cast<const T*>(q), static_cast<const T*>(k), static_cast<const T*>(v), static_cast<T*>(o), lse,
-        t->B * t->H, t->S_q, t->S_k, t->D, t->D_v, t->scale, t->maskType);
+        t->B * t->H, t->S_q, t->S_k, t->D, t->D_v, t->scale, t->maskType, t->H / kv_heads);
     t_last_path = 2;
     return check_launch("fa_fwd_simt_kernel");
 }
@@ -743,11 +745,13 @@ int launch_simt(const void* q, const void* k, const void* v, void* o, float* lse
 
 using namespace hc;
 
-extern "C" int hc_flash_attention_fwd_fused_launch(const void* q, const void* k, const void* v, void* o, float* lse,
-                                                   const flash_attention_fwd_fused_tiling_data* t, int dtype,
-                                                   void* stream) {
+extern "C" int hc_flash_attention_fwd_fused_gqa_launch(const void* q, const void* k, const void* v, void* o,
+                                                       float* lse, const flash_attention_fwd_fused_tiling_data* t,
+                                                       uint32_t kv_heads, int dtype, void* stream) {
     if (!t) return fail(HC_ERR_INVALID, "flash_attention: null tiling");
     if (t->B == 0 || t->H == 0 || t->S_q == 0) return ok();
+    if (kv_heads == 0 || t->H % kv_heads != 0)
+        return fail(HC_ERR_INVALID, "flash_attention: kv_heads %u must divide H %u", kv_heads, t->H);
     if (!q || !k || !v || !o) return fail(HC_ERR_INVALID, "flash_attention: null pointer");
     if (t->S_k == 0) return fail(HC_ERR_INVALID, "flash_attention: S_k must be >= 1");
     if (t->D == 0 || t->D_v == 0 || t->D > 256 || t->D_v > 256)
@@ -759,15 +763,21 @@ extern "C" int hc_flash_attention_fwd_fused_launch(const void* q, const void* k,
     const bool tc_shape = t->D == fa::kHD && t->D_v == fa::kHD && t->scale > 0.f &&
                           aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
     if (dtype == HC_DTYPE_BF16) {
-        if (tc_shape) return fa::launch_tc<true>(q, k, v, o, lse, t, s);
-        return fa::launch_simt<bf16_t>(q, k, v, o, lse, t, s);
+        if (tc_shape) return fa::launch_tc<true>(q, k, v, o, lse, t, kv_heads, s);
+        return fa::launch_simt<bf16_t>(q, k, v, o, lse, t, kv_heads, s);
     }
     if (dtype == HC_DTYPE_F16) {
-        if (tc_shape) return fa::launch_tc<false>(q, k, v, o, lse, t, s);
-        return fa::launch_simt<f16_t>(q, k, v, o, lse, t, s);
+        if (tc_shape) return fa::launch_tc<false>(q, k, v, o, lse, t, kv_heads, s);
+        return fa::launch_simt<f16_t>(q, k, v, o, lse, t, kv_heads, s);
     }
-    if (dtype == HC_DTYPE_F32) return fa::launch_simt<float>(q, k, v, o, lse, t, s);
+    if (dtype == HC_DTYPE_F32) return fa::launch_simt<float>(q, k, v, o, lse, t, kv_heads, s);
     return fail(HC_ERR_UNSUPPORTED, "flash_attention: dtype %d not supported (BF16, F16, F32)", dtype);
+}
+
+extern "C" int hc_flash_attention_fwd_fused_launch(const void* q, const void* k, const void* v, void* o, float* lse,
+                                                   const flash_attention_fwd_fused_tiling_data* t, int dtype,
+                                                   void* stream) {
+    return hc_flash_attention_fwd_fused_gqa_launch(q, k, v, o, lse, t, t ? t->H : 1u, dtype, stream);
 }
 
 extern "C" int hc_flash_attention_last_path(void) { return fa::t_last_path; }

@@ -18,7 +18,7 @@
 //   hc::layer_norm(x, gamma, beta, eps)                         layer_norm_runner.hpp
 //   hc::rms_norm_rope_fused(x, weight, cos, sin, rotary_dim, eps, heads, rope_style)
 //   hc::matmul_bias(a, b, bias?)                                matmul_bias_runner.hpp
-//   hc::flash_attention_fwd_fused(q, k, v, scale, mask_type) -> (o, lse)
+//   hc::flash_attention_fwd_fused(q, k, v, scale, mask_type) -> (o, lse)   (k, v may have fewer heads: GQA)
 // Load with torch.ops.load_library("ascend-npu-harness_b200/lib/libhc_torch.so").
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -227,9 +227,11 @@ std::tuple<at::Tensor, at::Tensor> flash_attention_fwd_fused_cuda(const at::Tens
     check_input(k, "k");
     check_input(v, "v");
     TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "hc: flash attention tensors are [B, H, S, D]");
-    TORCH_CHECK(k.size(0) == q.size(0) && v.size(0) == q.size(0) && k.size(1) == q.size(1) && v.size(1) == q.size(1) &&
-                    k.size(3) == q.size(3) && v.size(2) == k.size(2),
+    TORCH_CHECK(k.size(0) == q.size(0) && v.size(0) == q.size(0) && v.size(1) == k.size(1) && k.size(3) == q.size(3) &&
+                    v.size(2) == k.size(2),
                 "hc: flash attention q, k, v shapes disagree");
+    TORCH_CHECK(k.size(1) >= 1 && q.size(1) % k.size(1) == 0,
+                "hc: flash attention K/V heads (", k.size(1), ") must divide the query heads (", q.size(1), ")");
     TORCH_CHECK(k.scalar_type() == q.scalar_type() && v.scalar_type() == q.scalar_type(),
                 "hc: flash attention q, k, v must share a dtype");
     c10::cuda::CUDAGuard guard(q.device());
@@ -238,8 +240,9 @@ std::tuple<at::Tensor, at::Tensor> flash_attention_fwd_fused_cuda(const at::Tens
     flash_attention_fwd_fused_tiling_data t{u32(q.size(0), "B"), u32(q.size(1), "H"), u32(q.size(2), "S_q"),
                                             u32(k.size(2), "S_k"), u32(q.size(3), "D"), u32(v.size(3), "D_v"),
                                             static_cast<float>(scale), u32(mask_type, "mask_type")};
-    ok_or_throw(hc_flash_attention_fwd_fused_launch(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                                                    lse.data_ptr<float>(), &t, dtype_code(q), stream_of(q)),
+    ok_or_throw(hc_flash_attention_fwd_fused_gqa_launch(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                                        lse.data_ptr<float>(), &t, u32(k.size(1), "kv_heads"),
+                                                        dtype_code(q), stream_of(q)),
                 "flash_attention_fwd_fused");
     return {o, lse};
 }

@@ -129,6 +129,8 @@ SIGNATURES = {
     "hc_matmul_bias_launch": (_i, [_vp, _vp, _vp, _vp, _P(MatmulBiasTiling), _i, _vp]),
     "hc_flash_attention_fwd_fused_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _P(FlashAttentionFwdFusedTiling), _i,
                                                  _vp]),
+    "hc_flash_attention_fwd_fused_gqa_launch": (_i, [_vp, _vp, _vp, _vp, _vp, _P(FlashAttentionFwdFusedTiling), _u32, _i,
+                                                 _vp]),
     "hc_flash_attention_fwd_fused_host_workspace_size": (_i, [_P(FlashAttentionFwdFusedTiling), _i, _P(_sz)]),
     "hc_flash_attention_fwd_fused_host": (_i, [_vp, _vp, _vp, _vp, _vp, _P(FlashAttentionFwdFusedTiling), _i, _vp,
                                                _sz, _vp]),
@@ -310,10 +312,12 @@ def matmul_bias(A, B, bias=None, out=None, stream=None):
 
 def flash_attention_fwd(q, k, v, causal: bool, scale: float | None = None, with_lse: bool = True, out=None,
                         lse=None, stream=None):
-    """O = softmax(Q K^T * scale [causal]) V for [B, H, S, D] tensors; returns (O, lse or None)."""
+    """O = softmax(Q K^T * scale [causal]) V for [B, H, S, D] tensors; returns (O, lse or None).
+    K and V may have fewer heads than Q (a divisor of H): grouped-query attention."""
     torch = _torch()
     B, H, S_q, D = q.shape
     S_k, D_v = k.shape[2], v.shape[3]
+    kv_heads = k.shape[1]  # < H: grouped-query attention (query head h reads K/V head h // (H // kv_heads))
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if out is None:
@@ -321,9 +325,14 @@ def flash_attention_fwd(q, k, v, causal: bool, scale: float | None = None, with_
     if with_lse and lse is None:
         lse = torch.empty((B, H, S_q), dtype=torch.float32, device=q.device)
     t = FlashAttentionFwdFusedTiling(B, H, S_q, S_k, D, D_v, scale, 1 if causal else 0)
-    check(load().hc_flash_attention_fwd_fused_launch(_ptr(q), _ptr(k), _ptr(v), _ptr(out),
-                                                     _ptr(lse) if with_lse else None, C.byref(t), dtype_code(q),
-                                                     _stream(stream)))
+    if kv_heads == H:
+        check(load().hc_flash_attention_fwd_fused_launch(_ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                                                         _ptr(lse) if with_lse else None, C.byref(t), dtype_code(q),
+                                                         _stream(stream)))
+    else:
+        check(load().hc_flash_attention_fwd_fused_gqa_launch(_ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                                                             _ptr(lse) if with_lse else None, C.byref(t), kv_heads,
+                                                             dtype_code(q), _stream(stream)))
     return out, (lse if with_lse else None)
 
 

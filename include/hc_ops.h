@@ -203,6 +203,17 @@ int hc_flash_attention_fwd_fused_launch(const void* q, const void* k, const void
                                         const struct flash_attention_fwd_fused_tiling_data* t,
                                         int dtype, void* stream);
 
+/* Grouped-query form of the same kernel: K and V hold kv_heads heads ([B,kv_heads,S_k,D] and
+ * [B,kv_heads,S_k,D_v]), and query head h reads K/V head h / (H / kv_heads).  kv_heads must
+ * divide H (HC_ERR_INVALID otherwise, checked before any device work); kv_heads == H is
+ * hc_flash_attention_fwd_fused_launch.  No counterpart in the reference: its tiling record has
+ * no K/V head count, so this is an extra entry point rather than a change to the reference's
+ * launch ABI. */
+int hc_flash_attention_fwd_fused_gqa_launch(const void* q, const void* k, const void* v, void* o,
+                                            float* lse,
+                                            const struct flash_attention_fwd_fused_tiling_data* t,
+                                            uint32_t kv_heads, int dtype, void* stream);
+
 /* End-to-end variant with HOST buffers (pinned or pageable): copies q/k/v in, runs the kernel
  * and copies o/lse out, pipelined over chunks of (b,h) heads so that transfers overlap the
  * kernel.  `workspace` is a device buffer of at least

@@ -76,6 +76,11 @@ def test_host_side_validation_needs_no_gpu(hc_lib):
     assert lib.hc_matmul_bias_launch(fake, fake, None, fake, C.byref(mt), 2, None) == hc_lib.HC_ERR_INVALID
     et = hc_lib.ElementwiseAddTiling(16, 0)
     assert lib.hc_elementwise_add_launch(fake, fake, fake, C.byref(et), 9, None) == hc_lib.HC_ERR_UNSUPPORTED
+    gt = hc_lib.FlashAttentionFwdFusedTiling(1, 8, 16, 16, 128, 128, 0.1, 0)
+    for kv_heads in (0, 3, 16):  # must divide H = 8
+        assert lib.hc_flash_attention_fwd_fused_gqa_launch(fake, fake, fake, fake, None, C.byref(gt), kv_heads, 2,
+                                                           None) == hc_lib.HC_ERR_INVALID
+        assert b"kv_heads" in lib.hc_last_error_string()
 
 
 def test_fault_injection_is_reported_not_hidden(hc_lib):

@@ -11,7 +11,8 @@ fp64), restated in oracle/oracle.cpp with an added lse output.
   * the full benchmarked configuration B=16 H=32 S=8192 D=128 (causal and non-causal) against the
     independent fp32-math SIMT kernel on sampled heads, plus size-independent properties;
   * the host-buffer runner against the device entry point (bit-identical);
-  * the bounded-wait machinery reporting an expired wait as HC_ERR_TIMEOUT.
+  * the bounded-wait machinery reporting an expired wait as HC_ERR_TIMEOUT;
+  * grouped-query attention (K/V with fewer heads) on both kernels.
 """
 from __future__ import annotations
 
@@ -129,6 +130,49 @@ def test_tensor_core_ragged_shapes(cuda, hc_lib, oracle, shape, kind):
     ref, ref_lse = oracle.flash_attention_fwd(*(quantize(a, kind, oracle) for a in (q, k, v)), sc, causal, threads=8)
     assert_close(ref, o, O_TOL_BF16 if kind == "bf16" else 5e-3, 0.0, f"{kind} {shape}")
     assert_close(ref_lse, lse, LSE_TOL, 0.0, f"lse {shape}")
+
+
+@pytest.mark.parametrize("shape", [(2, 8, 2, 300, 300, 1), (1, 4, 1, 512, 700, 0), (1, 6, 3, 257, 257, 1),
+                                   (2, 4, 2, 128, 64, 0)],
+                         ids=lambda s: "B{}_H{}_Hkv{}_Sq{}_Sk{}_{}".format(*s[:5], "causal" if s[5] else "none"))
+@pytest.mark.parametrize("kind", ["bf16", "f16"])
+def test_grouped_query_attention(cuda, hc_lib, oracle, shape, kind):
+    """K/V with H_kv < H heads (hc_flash_attention_fwd_fused_gqa_launch): against the oracle on K/V
+    heads repeated H / H_kv times, and bit-identical to the tensor-core kernel run on that repeated copy."""
+    import torch
+
+    B, H, Hkv, Sq, Sk, causal = shape
+    D, g = 128, H // Hkv
+    q = oracle.normal(B * H * Sq * D, 20).reshape(B, H, Sq, D)
+    k = oracle.normal(B * Hkv * Sk * D, 21).reshape(B, Hkv, Sk, D)
+    v = oracle.normal(B * Hkv * Sk * D, 22).reshape(B, Hkv, Sk, D)
+    sc = C.default_scale(D)
+    o, lse = run_gpu(hc_lib, oracle, q, k, v, causal, kind, sc)
+    assert hc_lib.load().hc_flash_attention_last_path() == 1
+    kx, vx = np.repeat(k, g, axis=1), np.repeat(v, g, axis=1)
+    ref, ref_lse = oracle.flash_attention_fwd(*(quantize(a, kind, oracle) for a in (q, kx, vx)), sc, causal, threads=8)
+    assert_close(ref, o, O_TOL_BF16 if kind == "bf16" else 5e-3, 0.0, f"gqa {kind} {shape}")
+    assert_close(ref_lse, lse, LSE_TOL, 0.0, f"gqa lse {shape}")
+    o_mha, lse_mha = run_gpu(hc_lib, oracle, q, kx, vx, causal, kind, sc)
+    assert np.array_equal(o, o_mha) and np.array_equal(lse, lse_mha)
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("kind", ["f32", "bf16"])
+def test_grouped_query_attention_simt(cuda, hc_lib, oracle, kind):
+    """D = 64 GQA takes the SIMT kernel, which maps heads the same way."""
+    B, H, Hkv, S, D = 1, 4, 2, 96, 64
+    q = oracle.uniform(B * H * S * D, 30).reshape(B, H, S, D)
+    k = oracle.uniform(B * Hkv * S * D, 31).reshape(B, Hkv, S, D)
+    v = oracle.uniform(B * Hkv * S * D, 32).reshape(B, Hkv, S, D)
+    sc = C.default_scale(D)
+    o, lse = run_gpu(hc_lib, oracle, q, k, v, 1, kind, sc)
+    assert hc_lib.load().hc_flash_attention_last_path() == 2
+    kx, vx = np.repeat(k, 2, axis=1), np.repeat(v, 2, axis=1)
+    ref, ref_lse = oracle.flash_attention_fwd(*(quantize(a, kind, oracle) for a in (q, kx, vx)), sc, 1)
+    tol = 5e-4 if kind == "f32" else O_TOL_BF16
+    assert_close(ref, o, tol, 0.0, f"gqa simt {kind}")
+    assert_close(ref_lse, lse, 1e-3, 0.0, f"gqa simt lse {kind}")
 
 
 def test_large_logits_lazy_rescale(cuda, hc_lib, oracle):

@@ -115,6 +115,10 @@ def test_ops_match_ctypes_binding(ops):
     o, lse = ops.flash_attention_fwd_fused(q, k, v, 1 / math.sqrt(128), 1)
     o2, lse2 = hc.flash_attention_fwd(q, k, v, True)
     assert eq(o, o2) and torch.equal(lse, lse2)
+    kg, vg = rnd(1, 2, 300, 128), rnd(1, 2, 300, 128)  # grouped-query: 2 K/V heads for 4 query heads
+    o, lse = ops.flash_attention_fwd_fused(q, kg, vg, 1 / math.sqrt(128), 1)
+    o2, lse2 = hc.flash_attention_fwd(q, kg, vg, True)
+    assert eq(o, o2) and torch.equal(lse, lse2)
     torch.cuda.synchronize()
     hc.check_device_error()
 
