@@ -6,12 +6,13 @@
 // O = acc / l; causal masking hides key k from query q when k > q (golden.cpp:61-66).
 // Added output: lse = m + ln(l) per row (natural log), the standard flash-attention residual.
 //
-// Tensor-core path (bf16/fp16, D = D_v = 128), one persistent CTA per SM:
+// Tensor-core path (bf16/fp16, D = D_v = HD with HD 128 or 64), one persistent CTA per SM:
 //   * a CTA work unit is (b*h, block of 256 query rows) = two 128-row Q tiles;
 //   * warp 9 (producer) streams Q tiles and 128-key K/V tiles into shared memory with TMA
-//     (128-byte swizzle, a 4-stage K/V ring, no multicast);
-//   * warp 8 (one thread) issues tcgen05.mma: S_i = Q_i K^T into TMEM (M=128, N=128, K=16 x 8)
-//     and O_i += P_i V with P read straight from TMEM (the "TS" form), V as an MN-major operand;
+//     (128-byte swizzle, a 4-stage K/V ring at HD 128 and 8 stages at HD 64, no multicast);
+//   * warp 8 (one thread) issues tcgen05.mma: S_i = Q_i K^T into TMEM (M=128, N=128, K=16 x HD/16)
+//     and O_i += P_i V (N = HD) with P read straight from TMEM (the "TS" form), V as an MN-major
+//     operand;
 //   * warpgroups 0 and 1 each own one Q tile: thread t owns row t (TMEM lane t), reads its S row
 //     with tcgen05.ld, applies the causal / sequence-tail mask, updates (m, l) in the log2
 //     domain, writes P (16-bit) back over its S row with tcgen05.st, and rescales its O row in
@@ -20,7 +21,7 @@
 //   * the two Q tiles ping-pong: the tensor core runs one tile's MMAs while the other tile's
 //     softmax runs on the CUDA cores;
 //   * the epilogue (O / l -> 16-bit, lse) is done by the owning warpgroup from TMEM.
-// TMEM: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512) columns; P_i overlays S_i.
+// TMEM: S0 [0,128) S1 [128,256) O0 [256,256+HD) O1 [384,384+HD) columns; P_i overlays S_i.
 // Every mbarrier wait is bounded (4 s of global time): on expiry the kernel records the wait site
 // in a device error word, all roles unwind, in-flight copies and MMAs are drained, TMEM is freed,
 // and the host reports HC_ERR_TIMEOUT through hc_check_device_error().
@@ -46,16 +47,24 @@ using namespace sm100;
 
 constexpr uint32_t kBM = 128;      // query rows per Q tile
 constexpr uint32_t kBN = 128;      // keys per K/V tile
-constexpr uint32_t kHD = 128;      // head dim (D = D_v)
-constexpr uint32_t kStages = 4;    // K/V ring depth
 constexpr uint32_t kThreads = 384;
-constexpr uint32_t kTileBytes = kBM * kHD * 2;   // 32 KB, one 16-bit 128x128 tile
-constexpr uint32_t kHalfBytes = kTileBytes / 2;  // one 64-column swizzle panel
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffKV = 2 * kTileBytes;
-constexpr uint32_t kOffBar = kOffKV + kStages * kTileBytes;
-constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/misc + alignment slack
-constexpr float kRescaleThreshold = 8.0f;              // log2 units
+constexpr uint32_t kPanelBytes = kBM * 64 * 2;  // one 64-column swizzle panel of a 128-row tile: 16 KB
+constexpr float kRescaleThreshold = 8.0f;       // log2 units
+
+// Shared-memory geometry for head dimension HD (D = D_v = HD, 64 or 128).  A Q/K/V tile is 128
+// rows of HD 16-bit elements stored as HD / 64 panels of 128-byte swizzled rows; the K/V ring
+// is deeper when tiles are smaller.
+template <uint32_t HD>
+struct Geom {
+    static_assert(HD == 64 || HD == 128, "head dims 64 and 128");
+    static constexpr uint32_t kPanels = HD / 64;
+    static constexpr uint32_t kTileBytes = kPanels * kPanelBytes;
+    static constexpr uint32_t kStages = HD == 128 ? 4 : 8;  // K/V ring depth
+    static constexpr uint32_t kOffQ = 0;
+    static constexpr uint32_t kOffKV = 2 * kTileBytes;
+    static constexpr uint32_t kOffBar = kOffKV + kStages * kTileBytes;
+    static constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/misc + alignment slack
+};
 
 // Error word bits: which wait expired.
 enum : uint32_t {
@@ -80,6 +89,7 @@ struct Params {
     uint32_t causal;
 };
 
+template <uint32_t kStages>
 struct Bars {
     uint64_t q_full, q_empty;
     uint64_t kv_full[kStages], kv_empty[kStages];
@@ -221,20 +231,21 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 // word.  The MMAs are issued by one thread as a dependent chain, and a per-step rebuild of both
 // 64-bit descriptors made that chain long enough to leave the tensor pipe idle after each
 // softmax hand-off (4-5 % of the kernel's throughput on B200).
+template <uint32_t HD>
 __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr, uint32_t idesc) {
     const Sw128Desc qd = make_sw128_desc2(q_addr, 16, 1024), kd = make_sw128_desc2(k_addr, 16, 1024);
 #pragma unroll
-    for (uint32_t kk = 0; kk < kHD / 16; ++kk) {
+    for (uint32_t kk = 0; kk < HD / 16; ++kk) {
         // K-step kk: 16 columns = 32 B inside a 128-B swizzle row; the second 64-column half
-        // of the head lives kHalfBytes further on.
-        const uint32_t off = ((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4;
+        // of the head lives kPanelBytes further on.
+        const uint32_t off = ((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4;
         mma_ss2(d_tmem, Sw128Desc{qd.lo + off, qd.hi}, Sw128Desc{kd.lo + off, kd.hi}, idesc, kk > 0);
     }
 }
 
 __device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint32_t v_addr, uint32_t idesc,
                                          bool accumulate) {
-    const Sw128Desc vd = make_sw128_desc2(v_addr, kHalfBytes, 1024);
+    const Sw128Desc vd = make_sw128_desc2(v_addr, kPanelBytes, 1024);
 #pragma unroll
     for (uint32_t kk = 0; kk < kBN / 16; ++kk) {
         // 16 keys = 16 rows of the MN-major V panel = 2 swizzle atoms (2048 B); P: 8 columns.
@@ -243,14 +254,18 @@ __device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint3
     }
 }
 
-template <bool kBF16>
+template <bool kBF16, uint32_t HD>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const Params p) {
+    using G = Geom<HD>;
+    constexpr uint32_t kTileBytes = G::kTileBytes, kStages = G::kStages, kOffQ = G::kOffQ, kOffKV = G::kOffKV,
+                       kOffBar = G::kOffBar;
+    using BarsT = Bars<kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + sizeof(Bars));
+    BarsT* bars = reinterpret_cast<BarsT*>(smem + kOffBar);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + sizeof(BarsT));
     volatile uint32_t* abort_flag = tmem_slot + 1;
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
 
@@ -309,8 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 mbar_arrive_expect_tx(&bars->q_full, 2 * kTileBytes);
                 for (uint32_t i = 0; i < 2; ++i)
-                    for (uint32_t h = 0; h < 2; ++h)
-                        tma_load_3d(smem + kOffQ + i * kTileBytes + h * kHalfBytes, &tm_q, &bars->q_full,
+                    for (uint32_t h = 0; h < G::kPanels; ++h)
+                        tma_load_3d(smem + kOffQ + i * kTileBytes + h * kPanelBytes, &tm_q, &bars->q_full,
                                     static_cast<int32_t>(h * 64), static_cast<int32_t>(row0 + i * kBM),
                                     static_cast<int32_t>(bh));
                 q_pending = static_cast<int32_t>(q_iter & 1);
@@ -322,8 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             break;
                         }
                         mbar_arrive_expect_tx(&bars->kv_full[stage], kTileBytes);
-                        for (uint32_t h = 0; h < 2; ++h)
-                            tma_load_3d(smem + kOffKV + stage * kTileBytes + h * kHalfBytes, kv ? &tm_v : &tm_k,
+                        for (uint32_t h = 0; h < G::kPanels; ++h)
+                            tma_load_3d(smem + kOffKV + stage * kTileBytes + h * kPanelBytes, kv ? &tm_v : &tm_k,
                                         &bars->kv_full[stage], static_cast<int32_t>(h * 64),
                                         static_cast<int32_t>(j * kBN), static_cast<int32_t>(bh / p.group));
                         pend_valid |= 1u << stage;
@@ -351,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ==================================== MMA issuer ====================================
         if (lane == 0) {
             const uint32_t idesc_qk = make_idesc_f16(kBF16, kBM, kBN, false, false);
-            const uint32_t idesc_pv = make_idesc_f16(kBF16, kBM, kHD, false, true);
+            const uint32_t idesc_pv = make_idesc_f16(kBF16, kBM, HD, false, true);
             const uint32_t tS[2] = {tmem_base, tmem_base + 128};
             const uint32_t tO[2] = {tmem_base + 256, tmem_base + 384};
             const uint32_t qa[2] = {sQ, sQ + kTileBytes};
@@ -389,9 +404,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 uint32_t kst, vst;
                 if (!wait_kv(kst)) { ok = false; break; }
-                issue_qk(tS[0], qa[0], sKV + kst * kTileBytes, idesc_qk);
+                issue_qk<HD>(tS[0], qa[0], sKV + kst * kTileBytes, idesc_qk);
                 tc_commit(&bars->s_full[0]);
-                issue_qk(tS[1], qa[1], sKV + kst * kTileBytes, idesc_qk);
+                issue_qk<HD>(tS[1], qa[1], sKV + kst * kTileBytes, idesc_qk);
                 tc_commit(&bars->s_full[1]);
                 tc_commit(&bars->kv_empty[kst]);
                 if (nkv == 1) tc_commit(&bars->q_empty);
@@ -403,13 +418,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     if (!wait_kv(kst)) { ok = false; break; }            // K_j
                     if (j < n0) {
-                        issue_qk(tS[0], qa[0], sKV + kst * kTileBytes, idesc_qk);
+                        issue_qk<HD>(tS[0], qa[0], sKV + kst * kTileBytes, idesc_qk);
                         tc_commit(&bars->s_full[0]);
                     }
                     if (!wait_p(1)) { ok = false; break; }
                     issue_pv(tO[1], tS[1], sKV + vst * kTileBytes, idesc_pv, j - 1 > 0);
                     tc_commit(&bars->kv_empty[vst]);
-                    issue_qk(tS[1], qa[1], sKV + kst * kTileBytes, idesc_qk);
+                    issue_qk<HD>(tS[1], qa[1], sKV + kst * kTileBytes, idesc_qk);
                     tc_commit(&bars->s_full[1]);
                     tc_commit(&bars->kv_empty[kst]);
                     if (j + 1 == nkv) tc_commit(&bars->q_empty);
@@ -499,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // O row *= alpha (PV of the previous tile has completed: it was issued
                     // before the S MMA whose completion we just waited for).
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
+                    for (int c = 0; c < static_cast<int>(HD / 32); ++c) {
                         uint32_t orow[32];
                         tmem_ld32(tO + c * 32, orow);
                         tmem_wait_ld();
@@ -547,9 +562,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const float inv_l = 1.0f / l;
             const bool in_range = row < p.S_q;
-            uint8_t* orow_g = static_cast<uint8_t*>(p.o) + (static_cast<size_t>(bh) * p.S_q + row) * kHD * 2;
+            uint8_t* orow_g = static_cast<uint8_t*>(p.o) + (static_cast<size_t>(bh) * p.S_q + row) * HD * 2;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < static_cast<int>(HD / 32); ++c) {
                 uint32_t orow[32];
                 tmem_ld32(tO + c * 32, orow);
                 tmem_wait_ld();
@@ -676,9 +691,10 @@ uint32_t read_error_word(const char** name) {
 
 thread_local int t_last_path = 0;
 
-template <bool kBF16>
+template <bool kBF16, uint32_t HD>
 int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
               const flash_attention_fwd_fused_tiling_data* t, uint32_t kv_heads, cudaStream_t stream) {
+    constexpr uint32_t kSmemBytes = Geom<HD>::kSmemBytes;
     static std::once_flag reg_once;
     std::call_once(reg_once, [] { register_error_word(read_error_word); });
     const uint64_t BH = static_cast<uint64_t>(t->B) * t->H;
@@ -686,14 +702,14 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
     const CUtensorMapDataType dt = kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint32_t box[3] = {64, 128, 1};
     {
-        uint64_t dims[3] = {kHD, t->S_q, BH};
-        uint64_t strides[2] = {kHD * 2, static_cast<uint64_t>(t->S_q) * kHD * 2};
+        uint64_t dims[3] = {HD, t->S_q, BH};
+        uint64_t strides[2] = {HD * 2, static_cast<uint64_t>(t->S_q) * HD * 2};
         int rc = encode_tmap(&tmq, dt, 3, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
     {
-        uint64_t dims[3] = {kHD, t->S_k, static_cast<uint64_t>(t->B) * kv_heads};
-        uint64_t strides[2] = {kHD * 2, static_cast<uint64_t>(t->S_k) * kHD * 2};
+        uint64_t dims[3] = {HD, t->S_k, static_cast<uint64_t>(t->B) * kv_heads};
+        uint64_t strides[2] = {HD * 2, static_cast<uint64_t>(t->S_k) * HD * 2};
         int rc = encode_tmap(&tmk, dt, 3, k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
         rc = encode_tmap(&tmv, dt, 3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -712,16 +728,16 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
     prm.num_pairs = static_cast<uint32_t>(pairs);
     prm.scale_log2 = t->scale * 1.4426950408889634f;
     prm.causal = t->maskType;
-    static bool attr_set[2] = {false, false};
-    if (!attr_set[kBF16]) {
-        cudaError_t e = cudaFuncSetAttribute(fa_fwd_tc_kernel<kBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(fa_fwd_tc_kernel<kBF16, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kSmemBytes));
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fa_fwd_tc_kernel)");
-        attr_set[kBF16] = true;
+        attr_set = true;
     }
     uint32_t grid = static_cast<uint32_t>(sm_count());
     if (grid > prm.num_pairs) grid = prm.num_pairs;
-    fa_fwd_tc_kernel<kBF16><<<grid, kThreads, kSmemBytes, stream>>>(tmq, tmk, tmv, prm);
+    fa_fwd_tc_kernel<kBF16, HD><<<grid, kThreads, kSmemBytes, stream>>>(tmq, tmk, tmv, prm);
     t_last_path = 1;
     return check_launch("fa_fwd_tc_kernel");
 }
@@ -760,14 +776,16 @@ extern "C" int hc_flash_attention_fwd_fused_gqa_launch(const void* q, const void
     if (!std::isfinite(t->scale)) return fail(HC_ERR_INVALID, "flash_attention: scale must be finite");
     if (fault_hit("launch")) return fail(HC_ERR_INJECTED, "flash_attention: injected launch failure");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const bool tc_shape = t->D == fa::kHD && t->D_v == fa::kHD && t->scale > 0.f &&
-                          aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
+    const bool tc_shape = (t->D == 128 || t->D == 64) && t->D_v == t->D && t->scale > 0.f && aligned16(q) &&
+                          aligned16(k) && aligned16(v) && aligned16(o);
     if (dtype == HC_DTYPE_BF16) {
-        if (tc_shape) return fa::launch_tc<true>(q, k, v, o, lse, t, kv_heads, s);
+        if (tc_shape && t->D == 64) return fa::launch_tc<true, 64>(q, k, v, o, lse, t, kv_heads, s);
+        if (tc_shape) return fa::launch_tc<true, 128>(q, k, v, o, lse, t, kv_heads, s);
         return fa::launch_simt<bf16_t>(q, k, v, o, lse, t, kv_heads, s);
     }
     if (dtype == HC_DTYPE_F16) {
-        if (tc_shape) return fa::launch_tc<false>(q, k, v, o, lse, t, kv_heads, s);
+        if (tc_shape && t->D == 64) return fa::launch_tc<false, 64>(q, k, v, o, lse, t, kv_heads, s);
+        if (tc_shape) return fa::launch_tc<false, 128>(q, k, v, o, lse, t, kv_heads, s);
         return fa::launch_simt<f16_t>(q, k, v, o, lse, t, kv_heads, s);
     }
     if (dtype == HC_DTYPE_F32) return fa::launch_simt<float>(q, k, v, o, lse, t, kv_heads, s);

@@ -12,7 +12,8 @@ fp64), restated in oracle/oracle.cpp with an added lse output.
     independent fp32-math SIMT kernel on sampled heads, plus size-independent properties;
   * the host-buffer runner against the device entry point (bit-identical);
   * the bounded-wait machinery reporting an expired wait as HC_ERR_TIMEOUT;
-  * grouped-query attention (K/V with fewer heads) on both kernels.
+  * grouped-query attention (K/V with fewer heads) on both kernels;
+  * head dimension 64 on the tensor-core kernel.
 """
 from __future__ import annotations
 
@@ -56,8 +57,8 @@ def test_reference_cases_bf16(cuda, hc_lib, oracle, case):
     q, k, v = C.fa_inputs(oracle, B, H, Sq, Sk, D, Dv)
     sc = C.default_scale(D)
     o, lse = run_gpu(hc_lib, oracle, q, k, v, causal, "bf16", sc)
-    if D == 128 and Dv == 128:
-        assert hc_lib.load().hc_flash_attention_last_path() == 1, "D=128 must take the tcgen05 path"
+    if D == Dv and D in (64, 128):
+        assert hc_lib.load().hc_flash_attention_last_path() == 1, "D = D_v = 64 or 128 must take the tcgen05 path"
     qq, kq, vq = (quantize(a, "bf16", oracle) for a in (q, k, v))
     ref, ref_lse = oracle.flash_attention_fwd(qq, kq, vq, sc, causal)
     r = assert_close(ref, o, O_TOL_BF16, 0.0, f"bf16 {case}")
@@ -160,8 +161,8 @@ def test_grouped_query_attention(cuda, hc_lib, oracle, shape, kind):
 
 @pytest.mark.parametrize("kind", ["f32", "bf16"])
 def test_grouped_query_attention_simt(cuda, hc_lib, oracle, kind):
-    """D = 64 GQA takes the SIMT kernel, which maps heads the same way."""
-    B, H, Hkv, S, D = 1, 4, 2, 96, 64
+    """D = 32 GQA takes the SIMT kernel, which maps heads the same way."""
+    B, H, Hkv, S, D = 1, 4, 2, 96, 32
     q = oracle.uniform(B * H * S * D, 30).reshape(B, H, S, D)
     k = oracle.uniform(B * Hkv * S * D, 31).reshape(B, Hkv, S, D)
     v = oracle.uniform(B * Hkv * S * D, 32).reshape(B, Hkv, S, D)
@@ -173,6 +174,45 @@ def test_grouped_query_attention_simt(cuda, hc_lib, oracle, kind):
     tol = 5e-4 if kind == "f32" else O_TOL_BF16
     assert_close(ref, o, tol, 0.0, f"gqa simt {kind}")
     assert_close(ref_lse, lse, 1e-3, 0.0, f"gqa simt lse {kind}")
+
+
+@pytest.mark.parametrize("shape", [
+    (1, 3, 1000, 1000, 1), (2, 2, 300, 700, 0), (1, 1, 257, 257, 1), (1, 1, 1, 1, 0), (1, 2, 300, 200, 1),
+    (3, 5, 640, 640, 0), (1, 1, 513, 1024, 1),
+], ids=lambda s: "B{}_H{}_Sq{}_Sk{}_{}".format(*s[:4], "causal" if s[4] else "none"))
+@pytest.mark.parametrize("kind", ["bf16", "f16"])
+def test_tensor_core_head_dim_64(cuda, hc_lib, oracle, shape, kind):
+    """D = D_v = 64 on the tcgen05 kernel (one swizzle panel per tile, N = 64 P.V, 8-stage K/V ring)."""
+    B, H, Sq, Sk, causal = shape
+    D = 64
+    q = oracle.normal(B * H * Sq * D, 40).reshape(B, H, Sq, D)
+    k = oracle.normal(B * H * Sk * D, 41).reshape(B, H, Sk, D)
+    v = oracle.normal(B * H * Sk * D, 42).reshape(B, H, Sk, D)
+    sc = C.default_scale(D)
+    o, lse = run_gpu(hc_lib, oracle, q, k, v, causal, kind, sc)
+    assert hc_lib.load().hc_flash_attention_last_path() == 1
+    ref, ref_lse = oracle.flash_attention_fwd(*(quantize(a, kind, oracle) for a in (q, k, v)), sc, causal, threads=8)
+    assert_close(ref, o, O_TOL_BF16 if kind == "bf16" else 5e-3, 0.0, f"D64 {kind} {shape}")
+    assert_close(ref_lse, lse, LSE_TOL, 0.0, f"D64 lse {shape}")
+
+
+def test_tensor_core_head_dim_64_gqa_against_simt(cuda, hc_lib, oracle):
+    """D = 64 grouped-query causal on the tcgen05 kernel against the fp32-math SIMT kernel (fp32 inputs)."""
+    import torch
+
+    B, H, Hkv, S, D = 2, 8, 2, 1536, 64
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q = torch.randn(B, H, S, D, generator=g, device="cuda").to(torch.bfloat16)
+    k = torch.randn(B, Hkv, S, D, generator=g, device="cuda").to(torch.bfloat16)
+    v = torch.randn(B, Hkv, S, D, generator=g, device="cuda").to(torch.bfloat16)
+    o, lse = hc_lib.flash_attention_fwd(q, k, v, True)
+    assert hc_lib.load().hc_flash_attention_last_path() == 1
+    o32, lse32 = hc_lib.flash_attention_fwd(q.float(), k.float(), v.float(), True)
+    assert hc_lib.load().hc_flash_attention_last_path() == 2
+    torch.cuda.synchronize()
+    hc_lib.check_device_error()
+    assert (o.float() - o32).abs().max().item() <= O_TOL_BF16
+    assert (lse - lse32).abs().max().item() <= LSE_TOL
 
 
 def test_large_logits_lazy_rescale(cuda, hc_lib, oracle):
