@@ -6,12 +6,12 @@
 // O = acc / l; causal masking hides key k from query q when k > q (golden.cpp:61-66).
 // Added output: lse = m + ln(l) per row (natural log), the standard flash-attention residual.
 //
-// Tensor-core path (bf16/fp16, D = D_v = HD with HD 128 or 64), one persistent CTA per SM:
+// Tensor-core path (bf16/fp16, D = HD and D_v = HDV, each 128 or 64), one persistent CTA per SM:
 //   * a CTA work unit is (b*h, block of 256 query rows) = two 128-row Q tiles;
 //   * warp 9 (producer) streams Q tiles and 128-key K/V tiles into shared memory with TMA
 //     (128-byte swizzle, a 4-stage K/V ring at HD 128 and 8 stages at HD 64, no multicast);
 //   * warp 8 (one thread) issues tcgen05.mma: S_i = Q_i K^T into TMEM (M=128, N=128, K=16 x HD/16)
-//     and O_i += P_i V (N = HD) with P read straight from TMEM (the "TS" form), V as an MN-major
+//     and O_i += P_i V (N = HDV) with P read straight from TMEM (the "TS" form), V as an MN-major
 //     operand;
 //   * warpgroups 0 and 1 each own one Q tile: thread t owns row t (TMEM lane t), reads its S row
 //     with tcgen05.ld, applies the causal / sequence-tail mask, updates (m, l) in the log2
@@ -21,7 +21,7 @@
 //   * the two Q tiles ping-pong: the tensor core runs one tile's MMAs while the other tile's
 //     softmax runs on the CUDA cores;
 //   * the epilogue (O / l -> 16-bit, lse) is done by the owning warpgroup from TMEM.
-// TMEM: S0 [0,128) S1 [128,256) O0 [256,256+HD) O1 [384,384+HD) columns; P_i overlays S_i.
+// TMEM: S0 [0,128) S1 [128,256) O0 [256,256+HDV) O1 [384,384+HDV) columns; P_i overlays S_i.
 // Every mbarrier wait is bounded (4 s of global time): on expiry the kernel records the wait site
 // in a device error word, all roles unwind, in-flight copies and MMAs are drained, TMEM is freed,
 // and the host reports HC_ERR_TIMEOUT through hc_check_device_error().
@@ -51,18 +51,22 @@ constexpr uint32_t kThreads = 384;
 constexpr uint32_t kPanelBytes = kBM * 64 * 2;  // one 64-column swizzle panel of a 128-row tile: 16 KB
 constexpr float kRescaleThreshold = 8.0f;       // log2 units
 
-// Shared-memory geometry for head dimension HD (D = D_v = HD, 64 or 128).  A Q/K/V tile is 128
-// rows of HD 16-bit elements stored as HD / 64 panels of 128-byte swizzled rows; the K/V ring
-// is deeper when tiles are smaller.
-template <uint32_t HD>
+// Shared-memory geometry for Q/K head dimension HD and V/O head dimension HDV (each 64 or 128).
+// A tile is 128 rows of 16-bit elements stored as 64-column panels of 128-byte swizzled rows;
+// K and V tiles alternate in one ring whose slots hold the larger of the two, and the ring is
+// deeper when slots are smaller.
+template <uint32_t HD, uint32_t HDV>
 struct Geom {
-    static_assert(HD == 64 || HD == 128, "head dims 64 and 128");
-    static constexpr uint32_t kPanels = HD / 64;
+    static_assert((HD == 64 || HD == 128) && (HDV == 64 || HDV == 128), "head dims 64 and 128");
+    static constexpr uint32_t kPanels = HD / 64;    // Q and K tiles
+    static constexpr uint32_t kPanelsV = HDV / 64;  // V tiles
     static constexpr uint32_t kTileBytes = kPanels * kPanelBytes;
-    static constexpr uint32_t kStages = HD == 128 ? 4 : 8;  // K/V ring depth
+    static constexpr uint32_t kTileBytesV = kPanelsV * kPanelBytes;
+    static constexpr uint32_t kSlotBytes = kTileBytes > kTileBytesV ? kTileBytes : kTileBytesV;
+    static constexpr uint32_t kStages = kSlotBytes == kPanelBytes ? 8 : 4;  // K/V ring depth
     static constexpr uint32_t kOffQ = 0;
     static constexpr uint32_t kOffKV = 2 * kTileBytes;
-    static constexpr uint32_t kOffBar = kOffKV + kStages * kTileBytes;
+    static constexpr uint32_t kOffBar = kOffKV + kStages * kSlotBytes;
     static constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers/misc + alignment slack
 };
 
@@ -254,13 +258,13 @@ __device__ __forceinline__ void issue_pv(uint32_t o_tmem, uint32_t p_tmem, uint3
     }
 }
 
-template <bool kBF16, uint32_t HD>
+template <bool kBF16, uint32_t HD, uint32_t HDV>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const Params p) {
-    using G = Geom<HD>;
-    constexpr uint32_t kTileBytes = G::kTileBytes, kStages = G::kStages, kOffQ = G::kOffQ, kOffKV = G::kOffKV,
-                       kOffBar = G::kOffBar;
+    using G = Geom<HD, HDV>;
+    constexpr uint32_t kTileBytes = G::kTileBytes, kSlotBytes = G::kSlotBytes, kStages = G::kStages, kOffQ = G::kOffQ,
+                       kOffKV = G::kOffKV, kOffBar = G::kOffBar;
     using BarsT = Bars<kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -336,9 +340,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                             ok = false;
                             break;
                         }
-                        mbar_arrive_expect_tx(&bars->kv_full[stage], kTileBytes);
-                        for (uint32_t h = 0; h < G::kPanels; ++h)
-                            tma_load_3d(smem + kOffKV + stage * kTileBytes + h * kPanelBytes, kv ? &tm_v : &tm_k,
+                        mbar_arrive_expect_tx(&bars->kv_full[stage], kv ? G::kTileBytesV : kTileBytes);
+                        for (uint32_t h = 0; h < (kv ? G::kPanelsV : G::kPanels); ++h)
+                            tma_load_3d(smem + kOffKV + stage * kSlotBytes + h * kPanelBytes, kv ? &tm_v : &tm_k,
                                         &bars->kv_full[stage], static_cast<int32_t>(h * 64),
                                         static_cast<int32_t>(j * kBN), static_cast<int32_t>(bh / p.group));
                         pend_valid |= 1u << stage;
@@ -366,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ==================================== MMA issuer ====================================
         if (lane == 0) {
             const uint32_t idesc_qk = make_idesc_f16(kBF16, kBM, kBN, false, false);
-            const uint32_t idesc_pv = make_idesc_f16(kBF16, kBM, HD, false, true);
+            const uint32_t idesc_pv = make_idesc_f16(kBF16, kBM, HDV, false, true);
             const uint32_t tS[2] = {tmem_base, tmem_base + 128};
             const uint32_t tO[2] = {tmem_base + 256, tmem_base + 384};
             const uint32_t qa[2] = {sQ, sQ + kTileBytes};
@@ -404,9 +408,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 uint32_t kst, vst;
                 if (!wait_kv(kst)) { ok = false; break; }
-                issue_qk<HD>(tS[0], qa[0], sKV + kst * kTileBytes, idesc_qk);
+                issue_qk<HD>(tS[0], qa[0], sKV + kst * kSlotBytes, idesc_qk);
                 tc_commit(&bars->s_full[0]);
-                issue_qk<HD>(tS[1], qa[1], sKV + kst * kTileBytes, idesc_qk);
+                issue_qk<HD>(tS[1], qa[1], sKV + kst * kSlotBytes, idesc_qk);
                 tc_commit(&bars->s_full[1]);
                 tc_commit(&bars->kv_empty[kst]);
                 if (nkv == 1) tc_commit(&bars->q_empty);
@@ -414,17 +418,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!wait_kv(vst)) { ok = false; break; }            // V_{j-1}
                     if (j - 1 < n0) {
                         if (!wait_p(0)) { ok = false; break; }
-                        issue_pv(tO[0], tS[0], sKV + vst * kTileBytes, idesc_pv, j - 1 > 0);
+                        issue_pv(tO[0], tS[0], sKV + vst * kSlotBytes, idesc_pv, j - 1 > 0);
                     }
                     if (!wait_kv(kst)) { ok = false; break; }            // K_j
                     if (j < n0) {
-                        issue_qk<HD>(tS[0], qa[0], sKV + kst * kTileBytes, idesc_qk);
+                        issue_qk<HD>(tS[0], qa[0], sKV + kst * kSlotBytes, idesc_qk);
                         tc_commit(&bars->s_full[0]);
                     }
                     if (!wait_p(1)) { ok = false; break; }
-                    issue_pv(tO[1], tS[1], sKV + vst * kTileBytes, idesc_pv, j - 1 > 0);
+                    issue_pv(tO[1], tS[1], sKV + vst * kSlotBytes, idesc_pv, j - 1 > 0);
                     tc_commit(&bars->kv_empty[vst]);
-                    issue_qk<HD>(tS[1], qa[1], sKV + kst * kTileBytes, idesc_qk);
+                    issue_qk<HD>(tS[1], qa[1], sKV + kst * kSlotBytes, idesc_qk);
                     tc_commit(&bars->s_full[1]);
                     tc_commit(&bars->kv_empty[kst]);
                     if (j + 1 == nkv) tc_commit(&bars->q_empty);
@@ -433,11 +437,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!wait_kv(vst)) { ok = false; break; }                // V_{nkv-1}
                 if (n0 == nkv) {
                     if (!wait_p(0)) { ok = false; break; }
-                    issue_pv(tO[0], tS[0], sKV + vst * kTileBytes, idesc_pv, nkv > 1);
+                    issue_pv(tO[0], tS[0], sKV + vst * kSlotBytes, idesc_pv, nkv > 1);
                 }
                 tc_commit(&bars->o_full[0]);
                 if (!wait_p(1)) { ok = false; break; }
-                issue_pv(tO[1], tS[1], sKV + vst * kTileBytes, idesc_pv, nkv > 1);
+                issue_pv(tO[1], tS[1], sKV + vst * kSlotBytes, idesc_pv, nkv > 1);
                 tc_commit(&bars->o_full[1]);
                 tc_commit(&bars->kv_empty[vst]);
             }
@@ -514,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // O row *= alpha (PV of the previous tile has completed: it was issued
                     // before the S MMA whose completion we just waited for).
 #pragma unroll
-                    for (int c = 0; c < static_cast<int>(HD / 32); ++c) {
+                    for (int c = 0; c < static_cast<int>(HDV / 32); ++c) {
                         uint32_t orow[32];
                         tmem_ld32(tO + c * 32, orow);
                         tmem_wait_ld();
@@ -562,9 +566,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const float inv_l = 1.0f / l;
             const bool in_range = row < p.S_q;
-            uint8_t* orow_g = static_cast<uint8_t*>(p.o) + (static_cast<size_t>(bh) * p.S_q + row) * HD * 2;
+            uint8_t* orow_g = static_cast<uint8_t*>(p.o) + (static_cast<size_t>(bh) * p.S_q + row) * HDV * 2;
 #pragma unroll
-            for (int c = 0; c < static_cast<int>(HD / 32); ++c) {
+            for (int c = 0; c < static_cast<int>(HDV / 32); ++c) {
                 uint32_t orow[32];
                 tmem_ld32(tO + c * 32, orow);
                 tmem_wait_ld();
@@ -691,10 +695,10 @@ uint32_t read_error_word(const char** name) {
 
 thread_local int t_last_path = 0;
 
-template <bool kBF16, uint32_t HD>
+template <bool kBF16, uint32_t HD, uint32_t HDV>
 int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
               const flash_attention_fwd_fused_tiling_data* t, uint32_t kv_heads, cudaStream_t stream) {
-    constexpr uint32_t kSmemBytes = Geom<HD>::kSmemBytes;
+    constexpr uint32_t kSmemBytes = Geom<HD, HDV>::kSmemBytes;
     static std::once_flag reg_once;
     std::call_once(reg_once, [] { register_error_word(read_error_word); });
     const uint64_t BH = static_cast<uint64_t>(t->B) * t->H;
@@ -712,7 +716,9 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
         uint64_t strides[2] = {HD * 2, static_cast<uint64_t>(t->S_k) * HD * 2};
         int rc = encode_tmap(&tmk, dt, 3, k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
-        rc = encode_tmap(&tmv, dt, 3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+        uint64_t dims_v[3] = {HDV, t->S_k, static_cast<uint64_t>(t->B) * kv_heads};
+        uint64_t strides_v[2] = {HDV * 2, static_cast<uint64_t>(t->S_k) * HDV * 2};
+        rc = encode_tmap(&tmv, dt, 3, v, dims_v, strides_v, box, CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
     Params prm;
@@ -730,16 +736,26 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
     prm.causal = t->maskType;
     static bool attr_set = false;
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(fa_fwd_tc_kernel<kBF16, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(fa_fwd_tc_kernel<kBF16, HD, HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kSmemBytes));
         if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fa_fwd_tc_kernel)");
         attr_set = true;
     }
     uint32_t grid = static_cast<uint32_t>(sm_count());
     if (grid > prm.num_pairs) grid = prm.num_pairs;
-    fa_fwd_tc_kernel<kBF16, HD><<<grid, kThreads, kSmemBytes, stream>>>(tmq, tmk, tmv, prm);
+    fa_fwd_tc_kernel<kBF16, HD, HDV><<<grid, kThreads, kSmemBytes, stream>>>(tmq, tmk, tmv, prm);
     t_last_path = 1;
     return check_launch("fa_fwd_tc_kernel");
+}
+
+// The tensor-core kernel for the (D, D_v) pair: each of 64 and 128.
+template <bool kBF16>
+int launch_tc_dims(const void* q, const void* k, const void* v, void* o, float* lse,
+                   const flash_attention_fwd_fused_tiling_data* t, uint32_t kv_heads, cudaStream_t stream) {
+    if (t->D == 128 && t->D_v == 128) return launch_tc<kBF16, 128, 128>(q, k, v, o, lse, t, kv_heads, stream);
+    if (t->D == 64 && t->D_v == 64) return launch_tc<kBF16, 64, 64>(q, k, v, o, lse, t, kv_heads, stream);
+    if (t->D == 128) return launch_tc<kBF16, 128, 64>(q, k, v, o, lse, t, kv_heads, stream);
+    return launch_tc<kBF16, 64, 128>(q, k, v, o, lse, t, kv_heads, stream);
 }
 
 template <typename T>
@@ -776,16 +792,14 @@ extern "C" int hc_flash_attention_fwd_fused_gqa_launch(const void* q, const void
     if (!std::isfinite(t->scale)) return fail(HC_ERR_INVALID, "flash_attention: scale must be finite");
     if (fault_hit("launch")) return fail(HC_ERR_INJECTED, "flash_attention: injected launch failure");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const bool tc_shape = (t->D == 128 || t->D == 64) && t->D_v == t->D && t->scale > 0.f && aligned16(q) &&
-                          aligned16(k) && aligned16(v) && aligned16(o);
+    const bool tc_shape = (t->D == 128 || t->D == 64) && (t->D_v == 128 || t->D_v == 64) && t->scale > 0.f &&
+                          aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
     if (dtype == HC_DTYPE_BF16) {
-        if (tc_shape && t->D == 64) return fa::launch_tc<true, 64>(q, k, v, o, lse, t, kv_heads, s);
-        if (tc_shape) return fa::launch_tc<true, 128>(q, k, v, o, lse, t, kv_heads, s);
+        if (tc_shape) return fa::launch_tc_dims<true>(q, k, v, o, lse, t, kv_heads, s);
         return fa::launch_simt<bf16_t>(q, k, v, o, lse, t, kv_heads, s);
     }
     if (dtype == HC_DTYPE_F16) {
-        if (tc_shape && t->D == 64) return fa::launch_tc<false, 64>(q, k, v, o, lse, t, kv_heads, s);
-        if (tc_shape) return fa::launch_tc<false, 128>(q, k, v, o, lse, t, kv_heads, s);
+        if (tc_shape) return fa::launch_tc_dims<false>(q, k, v, o, lse, t, kv_heads, s);
         return fa::launch_simt<f16_t>(q, k, v, o, lse, t, kv_heads, s);
     }
     if (dtype == HC_DTYPE_F32) return fa::launch_simt<float>(q, k, v, o, lse, t, kv_heads, s);

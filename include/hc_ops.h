@@ -194,8 +194,8 @@ int hc_matmul_bias_launch(const void* A, const void* B, const void* bias, void* 
 /* O = softmax(Q K^T * scale [+ causal mask]) V with Q [B,H,S_q,D], K [B,H,S_k,D],
  * V [B,H,S_k,D_v], O [B,H,S_q,D_v] contiguous; optional lse [B,H,S_q] fp32 = natural-log
  * log-sum-exp of the scaled, masked scores (may be NULL).
- * dtype BF16 or F16 with D == D_v == 128 or 64 (16-byte aligned buffers) -> tcgen05/TMEM kernel;
- * any other D/D_v (<= 256) or dtype F32 -> SIMT kernel.  S_k >= 1 required.
+ * dtype BF16 or F16 with D and D_v each 64 or 128 (16-byte aligned buffers) -> tcgen05/TMEM
+ * kernel; any other D/D_v (<= 256) or dtype F32 -> SIMT kernel.  S_k >= 1 required.
  * Replaces flash_attention_fwd_fused_kernel
  * (ops/flash_attention_fwd_fused/kernel/flash_attention_fwd_fused_kernel.cpp:319-333). */
 int hc_flash_attention_fwd_fused_launch(const void* q, const void* k, const void* v, void* o,

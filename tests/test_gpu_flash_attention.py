@@ -13,7 +13,7 @@ fp64), restated in oracle/oracle.cpp with an added lse output.
   * the host-buffer runner against the device entry point (bit-identical);
   * the bounded-wait machinery reporting an expired wait as HC_ERR_TIMEOUT;
   * grouped-query attention (K/V with fewer heads) on both kernels;
-  * head dimension 64 on the tensor-core kernel.
+  * head dimension 64, and D != D_v (64/128 either way), on the tensor-core kernel.
 """
 from __future__ import annotations
 
@@ -194,6 +194,29 @@ def test_tensor_core_head_dim_64(cuda, hc_lib, oracle, shape, kind):
     ref, ref_lse = oracle.flash_attention_fwd(*(quantize(a, kind, oracle) for a in (q, k, v)), sc, causal, threads=8)
     assert_close(ref, o, O_TOL_BF16 if kind == "bf16" else 5e-3, 0.0, f"D64 {kind} {shape}")
     assert_close(ref_lse, lse, LSE_TOL, 0.0, f"D64 lse {shape}")
+
+
+@pytest.mark.parametrize("dims", [(128, 64), (64, 128)], ids=lambda d: "D{}_Dv{}".format(*d))
+@pytest.mark.parametrize("shape", [(1, 2, 300, 300, 1, 2), (2, 2, 257, 400, 0, 2), (1, 4, 513, 513, 1, 1),
+                                   (1, 1, 1, 1, 0, 1)],
+                         ids=lambda s: "B{}_H{}_Sq{}_Sk{}_{}_Hkv{}".format(*s[:4], "causal" if s[4] else "none", s[5]))
+@pytest.mark.parametrize("kind", ["bf16", "f16"])
+def test_tensor_core_value_dim_differs(cuda, hc_lib, oracle, dims, shape, kind):
+    """D != D_v on the tcgen05 kernel: Q/K tiles of D columns, V and O of D_v, K/V ring slots of the larger."""
+    D, Dv = dims
+    B, H, Sq, Sk, causal, Hkv = shape
+    q = oracle.normal(B * H * Sq * D, 50).reshape(B, H, Sq, D)
+    k = oracle.normal(B * Hkv * Sk * D, 51).reshape(B, Hkv, Sk, D)
+    v = oracle.normal(B * Hkv * Sk * Dv, 52).reshape(B, Hkv, Sk, Dv)
+    sc = C.default_scale(D)
+    o, lse = run_gpu(hc_lib, oracle, q, k, v, causal, kind, sc)
+    assert hc_lib.load().hc_flash_attention_last_path() == 1
+    g = H // Hkv
+    kx, vx = np.repeat(k, g, axis=1), np.repeat(v, g, axis=1)
+    ref, ref_lse = oracle.flash_attention_fwd(*(quantize(a, kind, oracle) for a in (q, kx, vx)), sc, causal, threads=8)
+    assert o.shape == (B, H, Sq, Dv)
+    assert_close(ref, o, O_TOL_BF16 if kind == "bf16" else 5e-3, 0.0, f"D{D} Dv{Dv} {kind} {shape}")
+    assert_close(ref_lse, lse, LSE_TOL, 0.0, f"D{D} Dv{Dv} lse {shape}")
 
 
 def test_tensor_core_head_dim_64_gqa_against_simt(cuda, hc_lib, oracle):
