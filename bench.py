@@ -187,6 +187,17 @@ class Dist:
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
+    def all_gather_into(self, out, t):
+        """out[r] = rank r's `t` on every rank (out has shape (world, *t.shape)).  NCCL gathers into
+        the one buffer; gloo, which has no single-buffer form, gathers into its slices."""
+        if not self.dist:
+            out[0].copy_(t)
+            return
+        if self.backend == "nccl":
+            self.dist.all_gather_into_tensor(out, t.contiguous())
+        else:
+            self.dist.all_gather(list(out.unbind(0)), t.contiguous())
+
     def close(self):
         if self.dist:
             self.dist.barrier()
@@ -366,6 +377,23 @@ def run_ours(args):
                 "peak_source": f"{peak_src} bf16_tflops (burst: the kernel is timed alone)",
                 "traffic": profile_traffic("flash_attention_fwd_causal"),
                 "algorithmic_flops_per_launch": flops_rank}
+
+    # ---------------- optional: the sharded outputs gathered onto every rank (after timing) -----------
+    gather = None
+    if args.gather_outputs and n > 1:
+        full = torch.empty((n,) + tuple(o.shape), dtype=o.dtype, device=dev)
+        d.barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        d.all_gather_into(full, o)
+        g1.record()
+        torch.cuda.synchronize()
+        g_ms = d.max(g0.elapsed_time(g1))
+        own_ok = 1.0 - d.max(0.0 if torch.equal(full[d.rank], o) else 1.0)  # 1 only if every rank's slice is its own O
+        gather = {"what": f"O [{fa_b}, {FA_H}, {FA_S}, {FA_D}] bf16 of every rank onto every rank (NCCL all-gather)",
+                  "bytes_per_rank": o.numel() * 2, "gathered_bytes": full.numel() * 2, "ms": g_ms,
+                  "gb_per_s_in_per_rank": (n - 1) * o.numel() * 2 / (g_ms * 1e-3) / 1e9, "own_slices_equal": own_ok == 1.0}
+        del full
     del o
 
     # ---------------- e2e through the host-buffer C entry point -----------------------------------
@@ -418,6 +446,7 @@ def run_ours(args):
                        "l2": "inputs 3.2 GB per GPU > 126 MB L2; no flush needed"},
             "gpu_launches": args.steps,
             "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "ops": ops,
+            **({"gather": gather} if gather else {}),
             "device": torch.cuda.get_device_name(dev),
         }
         print(json.dumps(line), flush=True)
@@ -622,6 +651,8 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the non-headline configurations")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--gather-outputs", action="store_true",
+                    help="with N > 1: all-gather every rank's attention output after the timed region and report it")
     ap.add_argument("--fa-batch", type=int, default=FA_B,
                     help="attention batch per GPU (default 16, the benchmarked size; smaller only for profiling captures)")
     ap.add_argument("--only", choices=EXTRA_OPS, default=None,

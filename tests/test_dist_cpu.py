@@ -31,6 +31,15 @@ def _rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
         d = bench.Dist(world, backend="gloo", timeout_s=10.0)
         if mode == "die" and rank == 1:
             os._exit(3)  # leaves between steps, without joining the barrier
+        if mode == "gather":
+            import torch
+
+            out = torch.empty((world, 3, 4), dtype=torch.float32)
+            d.all_gather_into(out, torch.full((3, 4), float(rank)))
+            ok = all(torch.equal(out[r], torch.full((3, 4), float(r))) for r in range(world))
+            d.close()
+            q.put((rank, "ok" if ok else "bad gather", 0.0, 0.0))
+            return
         d.barrier()
         ms_local = 10.0 + 5.0 * rank  # rank 1 is the slow one
         ms = d.max(ms_local)
@@ -76,3 +85,11 @@ def test_dead_rank_makes_the_other_fail_not_hang():
     assert not alive, "a rank waited for good on a rank that died"
     res = {r[0]: r for r in out}
     assert 0 in res and res[0][1] == "error", out
+
+
+def test_output_all_gather_two_ranks():
+    """The sharded-output all-gather (bench.py --gather-outputs) on two gloo ranks: every rank ends up with every
+    rank's shard in rank order."""
+    out, alive = _run(2, "gather", 120)
+    assert not alive
+    assert sorted(r[:2] for r in out) == [(0, "ok"), (1, "ok")]
