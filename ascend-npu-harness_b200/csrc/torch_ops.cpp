@@ -271,8 +271,11 @@ at::Tensor rms_norm_rope_fused_meta(const at::Tensor& x, const at::Tensor&, cons
 at::Tensor matmul_bias_meta(const at::Tensor& a, const at::Tensor& b, const std::optional<at::Tensor>&) {
     return at::empty({a.size(0), b.size(1)}, a.options());
 }
-std::tuple<at::Tensor, at::Tensor> flash_attention_fwd_fused_meta(const at::Tensor& q, const at::Tensor&,
+std::tuple<at::Tensor, at::Tensor> flash_attention_fwd_fused_meta(const at::Tensor& q, const at::Tensor& k,
                                                                   const at::Tensor& v, double, int64_t) {
+    TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "hc: flash attention tensors are [B, H, S, D]");
+    TORCH_CHECK(k.size(1) >= 1 && q.size(1) % k.size(1) == 0,
+                "hc: flash attention K/V heads (", k.size(1), ") must divide the query heads (", q.size(1), ")");
     return {at::empty({q.size(0), q.size(1), q.size(2), v.size(3)}, q.options()),
             at::empty({q.size(0), q.size(1), q.size(2)}, q.options().dtype(at::kFloat))};
 }

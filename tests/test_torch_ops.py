@@ -66,6 +66,10 @@ def test_meta_shapes(ops):
     kv = torch.empty(2, 3, 70, 128, dtype=torch.bfloat16, **m)
     o, lse = ops.flash_attention_fwd_fused(q, kv, kv, 0.088, 1)
     assert o.shape == (2, 3, 100, 128) and lse.shape == (2, 3, 100) and lse.dtype == torch.float32
+    q6 = torch.empty(2, 6, 100, 128, dtype=torch.bfloat16, **m)  # grouped-query: 3 K/V heads for 6 query heads
+    assert ops.flash_attention_fwd_fused(q6, kv, kv, 0.088, 1)[0].shape == (2, 6, 100, 128)
+    with pytest.raises(RuntimeError, match="must divide"):
+        ops.flash_attention_fwd_fused(torch.empty(2, 4, 100, 128, dtype=torch.bfloat16, **m), kv, kv, 0.088, 1)
 
 
 def test_cpu_tensors_have_no_kernel(ops):
