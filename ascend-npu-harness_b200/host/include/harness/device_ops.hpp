@@ -204,11 +204,17 @@ void run_flash_attention_fwd_fused_cuda(const float* Q, const float* K, const fl
                                         Mask mask_type) {
     run_flash_attention_fwd_fused_cuda(Q, K, V, O, B, H, S_q, S_k, D, D_v, scale, device::detail::as_int(mask_type));
 }
-// Device buffers; lse [B,H,S_q] fp32 (natural log) may be nullptr.  bf16/fp16 with
-// D == D_v == 128 runs the tcgen05/TMEM kernel.
+// Device buffers; lse [B,H,S_q] fp32 (natural log) may be nullptr.  bf16/fp16 with D and D_v
+// each 64 or 128 runs the tcgen05/TMEM kernel.
 void run_flash_attention_fwd_fused_device(const void* q, const void* k, const void* v, void* o, float* lse,
                                           int64_t B, int64_t H, int64_t S_q, int64_t S_k, int64_t D, int64_t D_v,
                                           float scale, int mask_type, device::Dtype dtype, void* stream = nullptr);
+// Grouped-query form (no counterpart in the reference): K and V hold kv_heads heads, a divisor of
+// H, and query head h reads K/V head h / (H / kv_heads).
+void run_flash_attention_fwd_fused_gqa_device(const void* q, const void* k, const void* v, void* o, float* lse,
+                                              int64_t B, int64_t H, int64_t kv_heads, int64_t S_q, int64_t S_k,
+                                              int64_t D, int64_t D_v, float scale, int mask_type, device::Dtype dtype,
+                                              void* stream = nullptr);
 // Host buffers of `dtype` (pinned for full copy bandwidth); copies are pipelined with the kernel
 // over chunks of heads.  Synchronous: returns when o and lse are in host memory.
 void run_flash_attention_fwd_fused_host(const void* q, const void* k, const void* v, void* o, float* lse,

@@ -379,6 +379,19 @@ void run_flash_attention_fwd_fused_device(const void* q, const void* k, const vo
                  "flash_attention_fwd_fused");
 }
 
+void run_flash_attention_fwd_fused_gqa_device(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B,
+                                              int64_t H, int64_t kv_heads, int64_t S_q, int64_t S_k, int64_t D,
+                                              int64_t D_v, float scale, int mask_type, Dtype dtype, void* stream) {
+    const char* what = "flash_attention_fwd_fused (grouped-query)";
+    const auto t = fa_tiling(B, H, S_q, S_k, D, D_v, scale, mask_type);
+    if (kv_heads <= 0 || H % kv_heads != 0)
+        throw DeviceError(HC_ERR_INVALID, "flash_attention_fwd_fused: kv_heads must divide H");
+    if (B * H * S_q == 0) return;
+    ThrowIfError(hc_flash_attention_fwd_fused_gqa_launch(q, k, v, o, lse, &t, u32(kv_heads, what), static_cast<int>(dtype),
+                                                         stream),
+                 what);
+}
+
 void run_flash_attention_fwd_fused_cuda(const float* Q, const float* K, const float* V, float* O, int64_t B, int64_t H,
                                         int64_t S_q, int64_t S_k, int64_t D, int64_t D_v, float scale, int mask_type) {
     const char* what = "flash_attention_fwd_fused";

@@ -417,6 +417,31 @@ TEST(FlashAttentionTest, Bf16SubsliceOnTensorCores) {  // B=1 H=2 S=1024 D=128, 
     }
 }
 
+TEST(FlashAttentionTest, GroupedQueryMatchesRepeatedHeads) {
+    // 8 query heads over 2 K/V heads, D 128 causal: the same bits as the per-head runner given each K/V head repeated 4x
+    const int64_t B = 2, H = 8, Hkv = 2, S = 300, D = 128, g = H / Hkv;
+    const size_t nq = prod({B, H, S, D}), nkv = prod({B, Hkv, S, D});
+    auto qq = to_bf16(normal(nq, 20)), kq = to_bf16(normal(nkv, 21)), vq = to_bf16(normal(nkv, 22));
+    std::vector<uint16_t> kx(nq), vx(nq);
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t h = 0; h < H; ++h)
+            for (int64_t e = 0; e < S * D; ++e) {
+                kx[((b * H + h) * S * D) + e] = kq[((b * Hkv + h / g) * S * D) + e];
+                vx[((b * H + h) * S * D) + e] = vq[((b * Hkv + h / g) * S * D) + e];
+            }
+    const float sc = default_scale(D);
+    DeviceMemory dq = upload(qq), dk = upload(kq), dv = upload(vq), dkx = upload(kx), dvx = upload(vx);
+    DeviceMemory o1(nq * 2), o2(nq * 2), l1(B * H * S * 4), l2(B * H * S * 4);
+    harness::flash_attention_fwd_fused::run_flash_attention_fwd_fused_gqa_device(
+        dq.data(), dk.data(), dv.data(), o1.data(), l1.as<float>(), B, H, Hkv, S, S, D, D, sc, 1, Dtype::BF16);
+    harness::flash_attention_fwd_fused::run_flash_attention_fwd_fused_device(
+        dq.data(), dkx.data(), dvx.data(), o2.data(), l2.as<float>(), B, H, S, S, D, D, sc, 1, Dtype::BF16);
+    ASSERT_TRUE(harness::device::DeviceSynchronize());
+    ASSERT_TRUE(harness::device::CheckDeviceError());
+    EXPECT_TRUE(download<uint16_t>(o1, nq) == download<uint16_t>(o2, nq)) << "O bit-identical";
+    EXPECT_TRUE(download<float>(l1, B * H * S) == download<float>(l2, B * H * S)) << "lse bit-identical";
+}
+
 TEST(FlashAttentionTest, HostBufferRunnerMatchesDevice) {
     const int64_t B = 2, H = 5, S = 700, D = 128;
     const size_t n = prod({B, H, S, D});

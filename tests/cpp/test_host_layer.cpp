@@ -124,6 +124,13 @@ TEST(HostValidationTest, ArgumentsTheKernelsCannotTakeAreRejectedFirst) {
                       b.data(), b.data(), b.data(), b.data(), 1, 1, 1, 1, 2, 2, 0.5f, 2);
               }),
               HC_ERR_INVALID);
+    EXPECT_EQ(status_of([&] {
+                  harness::flash_attention_fwd_fused::run_flash_attention_fwd_fused_gqa_device(
+                      b.data(), b.data(), b.data(), b.data(), nullptr, 1, 8, 3, 16, 16, 128, 128, 0.5f, 1,
+                      harness::device::Dtype::BF16);
+              }),
+              HC_ERR_INVALID)
+        << "kv_heads must divide H (checked before any device work)";
     EXPECT_EQ(status_of([&] { harness::runner::reduce_sum_lastdim::run(b.data(), b.data(), 1, -1, 4); }), HC_ERR_INVALID);
     EXPECT_EQ(status_of([&] {
                   harness::matmul_bias::run_matmul_bias_cuda(b.data(), b.data(), nullptr, b.data(), int64_t(1) << 20,
