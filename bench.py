@@ -461,6 +461,16 @@ EXTRA_OPS = ("flash_attention_fwd_noncausal", "matmul_bias", "layer_norm", "rms_
 ANALOG_OPS = EXTRA_OPS[5:]
 
 
+def settle():
+    """Each configuration after the headline starts from an idle GPU: after the 8192^3 GEMM's power
+    burst the power controller holds the clock down for about a second, and the next kernel
+    (layer_norm here) measured up to 10 points low when timed at once."""
+    import torch
+
+    torch.cuda.synchronize()
+    time.sleep(1.0)
+
+
 def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
     """The other benchmarked configurations, each timed alone (W=3, 20 launches)."""
     import torch
@@ -475,13 +485,6 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
     # can neither re-read the previous launch's inputs nor rewrite its still-dirty outputs in L2.
     hbm = peaks["hbm_gbs"]
     flip = [0]
-
-    def settle():
-        """Each configuration starts from an idle GPU: after the 8192^3 GEMM's power burst the power controller
-        holds the clock down for about a second, and the next kernel (layer_norm here) measured up to 10 points
-        low when timed at once."""
-        torch.cuda.synchronize()
-        time.sleep(1.0)
 
     def alternate(sets):
         def nxt():
