@@ -35,6 +35,22 @@ int sm_count();
 // grid leaves its extra blocks a second, partly empty wave at the end of the launch.
 int resident_blocks(const void* kernel, int threads, size_t smem);
 
+// Raises `kernel`'s dynamic shared-memory limit to at least `bytes` on the current device.
+// cudaFuncSetAttribute acts on the current device's context only, so the setting is recorded per
+// (kernel, device) under a lock: each device gets it on its first launch from any host thread,
+// and threads driving different devices never share a flag.  Returns HC_OK or HC_ERR_CUDA
+// naming `name`.
+int set_max_dynamic_smem(const void* kernel, size_t bytes, const char* name);
+
+// Checks a flash-attention tiling record, K/V head count and element type without touching the
+// device (the checks hc_flash_attention_fwd_fused_gqa_launch makes before any launch).  An empty
+// problem (B, H or S_q zero) is valid.  Returns HC_OK or the error status with its message set.
+int fa_check_tiling(const flash_attention_fwd_fused_tiling_data* t, uint32_t kv_heads, int dtype);
+
+// Unique id of the calling thread's current CUDA context (stable for the context's lifetime and
+// never reused, unlike a device ordinal: a device reset gives the device a new id); 0 if unknown.
+uint64_t current_context_id();
+
 // Size in bytes of one element of an hc_dtype, 0 for an unknown value.
 size_t dtype_size(int dtype);
 

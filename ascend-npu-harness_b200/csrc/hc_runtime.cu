@@ -109,16 +109,69 @@ int resident_blocks(const void* kernel, int threads, size_t smem) {
 }
 
 int sm_count() {
-    static int cache[64] = {0};
+    static std::atomic<int> cache[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (cache[dev] == 0) {
-        int sms = 0;
+    int sms = cache[dev].load(std::memory_order_relaxed);
+    if (sms == 0) {
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
             sms = 148;
-        cache[dev] = sms;
+        cache[dev].store(sms, std::memory_order_relaxed);
     }
-    return cache[dev];
+    return sms;
+}
+
+uint64_t current_context_id() {
+    using GetCurrentFn = int (*)(void**);
+    using GetIdFn = int (*)(void*, unsigned long long*);
+    static std::once_flag once;
+    static GetCurrentFn get_current = nullptr;
+    static GetIdFn get_id = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrentFn>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetIdFn>(p);
+        cudaGetLastError();
+    });
+    if (!get_current || !get_id) return 0;
+    void* ctx = nullptr;  // none until the runtime has bound the device's primary context to the thread
+    unsigned long long id = 0;
+    if (get_current(&ctx) != 0 || !ctx || get_id(ctx, &id) != 0) return 0;
+    return static_cast<uint64_t>(id);
+}
+
+int set_max_dynamic_smem(const void* kernel, size_t bytes, const char* name) {
+    struct Entry {
+        const void* kernel;
+        int dev;
+        size_t bytes;
+    };
+    static std::mutex mu;
+    static std::vector<Entry> done;
+    int dev = 0;
+    HC_CHECK_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry& e : done)
+        if (e.kernel == kernel && e.dev == dev && e.bytes >= bytes) return HC_OK;
+    const cudaError_t err =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return fail(HC_ERR_CUDA, "cudaFuncSetAttribute(%s, %zu B) on device %d: %s", name, bytes, dev,
+                    cudaGetErrorString(err));
+    }
+    for (Entry& e : done)
+        if (e.kernel == kernel && e.dev == dev) {
+            e.bytes = bytes;
+            return HC_OK;
+        }
+    done.push_back(Entry{kernel, dev, bytes});
+    return HC_OK;
 }
 
 size_t dtype_size(int dtype) {

@@ -16,24 +16,31 @@ namespace hc {
 namespace {
 
 // Three internal streams per device (copy-in, compute, copy-out) and the events that chain them;
-// created once per device and kept for the life of the process.
+// created on a device's first call and kept while the device's context lives.  `mu` serialises
+// whole calls on one device: the events are shared, so two calls enqueuing at once could chain
+// one call's copies to the other's start.
 struct Pipe {
-    bool ready = false;
+    std::mutex mu;
+    uint64_t ctx = 0;  // context the handles belong to; a device reset makes them stale
     cudaStream_t in = nullptr, comp = nullptr, out = nullptr;
     cudaEvent_t in_done[2] = {nullptr, nullptr}, comp_done[2] = {nullptr, nullptr}, out_done[2] = {nullptr, nullptr};
     cudaEvent_t start = nullptr;
 };
 
-std::mutex g_pipe_mu;
 Pipe g_pipes[64];
 
-int get_pipe(Pipe** out) {
+// Returns the calling thread's device pipe with its mutex held in `lock`.
+int get_pipe(Pipe** out, std::unique_lock<std::mutex>* lock) {
     int dev = 0;
     HC_CHECK_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(HC_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
-    std::lock_guard<std::mutex> lk(g_pipe_mu);
     Pipe& p = g_pipes[dev];
-    if (!p.ready) {
+    *lock = std::unique_lock<std::mutex>(p.mu);
+    const uint64_t ctx = current_context_id();
+    if (p.ctx == 0 || ctx == 0 || p.ctx != ctx) {
+        // First use on this device, or the device was reset since (the old handles died with the
+        // old context and are dropped, not destroyed).
+        p.ctx = 0;
         HC_CHECK_CUDA(cudaStreamCreateWithFlags(&p.in, cudaStreamNonBlocking));
         HC_CHECK_CUDA(cudaStreamCreateWithFlags(&p.comp, cudaStreamNonBlocking));
         HC_CHECK_CUDA(cudaStreamCreateWithFlags(&p.out, cudaStreamNonBlocking));
@@ -43,7 +50,7 @@ int get_pipe(Pipe** out) {
             HC_CHECK_CUDA(cudaEventCreateWithFlags(&p.out_done[b], cudaEventDisableTiming));
         }
         HC_CHECK_CUDA(cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming));
-        p.ready = true;
+        p.ctx = current_context_id();
     }
     *out = &p;
     return HC_OK;
@@ -96,17 +103,36 @@ extern "C" int hc_flash_attention_fwd_fused_host(const void* h_q, const void* h_
                                                  int dtype, void* workspace, size_t workspace_bytes, void* stream) {
     if (!t) return fail(HC_ERR_INVALID, "flash_attention host: null tiling");
     if (!h_q || !h_k || !h_v || !h_o || !workspace) return fail(HC_ERR_INVALID, "flash_attention host: null pointer");
+    int rc = fa_check_tiling(t, t->H, dtype);
+    if (rc) return rc;
     FaChunking c;
-    int rc = fa_chunking(t, dtype, &c);
+    rc = fa_chunking(t, dtype, &c);
     if (rc) return rc;
     if (workspace_bytes < 2 * c.slot_bytes)
         return fail(HC_ERR_INVALID, "flash_attention host: workspace %zu B < required %llu B", workspace_bytes,
                     static_cast<unsigned long long>(2 * c.slot_bytes));
     if (c.bh == 0 || t->S_q == 0) return ok();
     Pipe* pp = nullptr;
-    rc = get_pipe(&pp);
+    std::unique_lock<std::mutex> pipe_lock;
+    rc = get_pipe(&pp, &pipe_lock);
     if (rc) return rc;
     Pipe& P = *pp;
+    cudaStream_t user = static_cast<cudaStream_t>(stream);
+    // Once anything is enqueued, an error return first waits for the work already queued on the
+    // internal streams: the caller may free the workspace or reuse the host buffers as soon as
+    // the call returns.
+    auto join = [&](int status) {
+        cudaStreamSynchronize(P.in);
+        cudaStreamSynchronize(P.comp);
+        cudaStreamSynchronize(P.out);
+        cudaGetLastError();
+        return status;
+    };
+#define HC_PIPE_CHECK(call)                                              \
+    do {                                                                 \
+        cudaError_t e__ = (call);                                        \
+        if (e__ != cudaSuccess) return join(cuda_fail(e__, #call));      \
+    } while (0)
     const size_t es = dtype_size(dtype);
     auto align = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
     const uint64_t h = c.heads_per_chunk;
@@ -115,9 +141,8 @@ extern "C" int hc_flash_attention_fwd_fused_host(const void* h_q, const void* h_
     uint8_t* slot[2];
     slot[0] = static_cast<uint8_t*>(workspace);
     slot[1] = slot[0] + c.slot_bytes;
-    cudaStream_t user = static_cast<cudaStream_t>(stream);
-    HC_CHECK_CUDA(cudaEventRecord(P.start, user));
-    HC_CHECK_CUDA(cudaStreamWaitEvent(P.in, P.start, 0));
+    HC_PIPE_CHECK(cudaEventRecord(P.start, user));
+    HC_PIPE_CHECK(cudaStreamWaitEvent(P.in, P.start, 0));
     const uint64_t nchunks = (c.bh + h - 1) / h;
     for (uint64_t ci = 0; ci < nchunks; ++ci) {
         const int b = static_cast<int>(ci & 1);
@@ -130,32 +155,33 @@ extern "C" int hc_flash_attention_fwd_fused_host(const void* h_q, const void* h_
         float* dl = reinterpret_cast<float*>(dO + align(h * c.o_head_bytes));
         // Copy-in of this chunk may start once the copy-out of the chunk that used this slot
         // two steps ago is finished (which also implies its kernel finished).
-        if (ci >= 2) HC_CHECK_CUDA(cudaStreamWaitEvent(P.in, P.out_done[b], 0));
-        if (fault_hit("memcpy")) return fail(HC_ERR_INJECTED, "flash_attention host: injected copy failure");
-        HC_CHECK_CUDA(cudaMemcpyAsync(dq, static_cast<const uint8_t*>(h_q) + h0 * c.q_head_bytes, hn * c.q_head_bytes,
+        if (ci >= 2) HC_PIPE_CHECK(cudaStreamWaitEvent(P.in, P.out_done[b], 0));
+        if (fault_hit("memcpy")) return join(fail(HC_ERR_INJECTED, "flash_attention host: injected copy failure"));
+        HC_PIPE_CHECK(cudaMemcpyAsync(dq, static_cast<const uint8_t*>(h_q) + h0 * c.q_head_bytes, hn * c.q_head_bytes,
                                       cudaMemcpyHostToDevice, P.in));
-        HC_CHECK_CUDA(cudaMemcpyAsync(dk, static_cast<const uint8_t*>(h_k) + h0 * k_bytes_h, hn * k_bytes_h,
+        HC_PIPE_CHECK(cudaMemcpyAsync(dk, static_cast<const uint8_t*>(h_k) + h0 * k_bytes_h, hn * k_bytes_h,
                                       cudaMemcpyHostToDevice, P.in));
-        HC_CHECK_CUDA(cudaMemcpyAsync(dv, static_cast<const uint8_t*>(h_v) + h0 * v_bytes_h, hn * v_bytes_h,
+        HC_PIPE_CHECK(cudaMemcpyAsync(dv, static_cast<const uint8_t*>(h_v) + h0 * v_bytes_h, hn * v_bytes_h,
                                       cudaMemcpyHostToDevice, P.in));
-        HC_CHECK_CUDA(cudaEventRecord(P.in_done[b], P.in));
-        HC_CHECK_CUDA(cudaStreamWaitEvent(P.comp, P.in_done[b], 0));
+        HC_PIPE_CHECK(cudaEventRecord(P.in_done[b], P.in));
+        HC_PIPE_CHECK(cudaStreamWaitEvent(P.comp, P.in_done[b], 0));
         flash_attention_fwd_fused_tiling_data tc = *t;
         tc.B = 1;
         tc.H = static_cast<uint32_t>(hn);
         rc = hc_flash_attention_fwd_fused_launch(dq, dk, dv, dO, h_lse ? dl : nullptr, &tc, dtype, P.comp);
-        if (rc) return rc;
-        HC_CHECK_CUDA(cudaEventRecord(P.comp_done[b], P.comp));
-        HC_CHECK_CUDA(cudaStreamWaitEvent(P.out, P.comp_done[b], 0));
-        HC_CHECK_CUDA(cudaMemcpyAsync(static_cast<uint8_t*>(h_o) + h0 * c.o_head_bytes, dO, hn * c.o_head_bytes,
+        if (rc) return join(rc);
+        HC_PIPE_CHECK(cudaEventRecord(P.comp_done[b], P.comp));
+        HC_PIPE_CHECK(cudaStreamWaitEvent(P.out, P.comp_done[b], 0));
+        HC_PIPE_CHECK(cudaMemcpyAsync(static_cast<uint8_t*>(h_o) + h0 * c.o_head_bytes, dO, hn * c.o_head_bytes,
                                       cudaMemcpyDeviceToHost, P.out));
         if (h_lse)
-            HC_CHECK_CUDA(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(h_lse) + h0 * c.lse_head_bytes, dl,
+            HC_PIPE_CHECK(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(h_lse) + h0 * c.lse_head_bytes, dl,
                                           hn * c.lse_head_bytes, cudaMemcpyDeviceToHost, P.out));
-        HC_CHECK_CUDA(cudaEventRecord(P.out_done[b], P.out));
+        HC_PIPE_CHECK(cudaEventRecord(P.out_done[b], P.out));
     }
-    HC_CHECK_CUDA(cudaStreamWaitEvent(user, P.out_done[(nchunks - 1) & 1], 0));
-    HC_CHECK_CUDA(cudaStreamSynchronize(P.out));
+    HC_PIPE_CHECK(cudaStreamWaitEvent(user, P.out_done[(nchunks - 1) & 1], 0));
+    HC_PIPE_CHECK(cudaStreamSynchronize(P.out));
+#undef HC_PIPE_CHECK
     return hc_check_device_error();
 }
 
@@ -169,9 +195,14 @@ extern "C" int hc_flash_attention_fwd_fused_host(const void* h_q, const void* h_
 // owned by their own pool or budget, where an allocation inside the call could fail or would
 // synchronise the device.
 //   * Limit: kNoAllocScratchBytes per device.  One head's staging (q, k, v, o, lse) must fit;
-//     larger heads are rejected with HC_ERR_UNSUPPORTED before any device work.
+//     larger heads, and every tiling the kernel would reject, are refused before any device work.
+//   * The array is part of the library's device image: every device that loads the library
+//     holds its 64 MiB until the process exits, whether or not this runner is ever called.
 //   * The first call on a device looks the array's address up with cudaGetSymbolAddress (and
-//     the kernel sets its attributes); make that first call before any stream capture.
+//     the kernel sets its attributes); make that first call before any stream capture.  The
+//     address is kept per device context, so a device reset leads to a fresh lookup.
+//   * The call waits for the caller's stream to drain before it returns, on success and on an
+//     error after its first copy alike, so the host buffers are free again on return.
 //   * Nothing in the scratch has to start at zero: every byte read is written earlier in the
 //     same call.
 //   * All calls on one device share the one array: calls that overlap in time (other threads,
@@ -184,20 +215,27 @@ constexpr size_t kNoAllocScratchBytes = 64ull << 20;  // 64 MiB per device
 static __device__ __align__(256) uint8_t g_fa_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {};
+struct ScratchAddr {
+    uint64_t ctx = 0;
+    void* ptr = nullptr;
+};
+ScratchAddr g_noalloc_addr[64];
 
 int noalloc_scratch(void** out) {
     int dev = 0;
     HC_CHECK_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(HC_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
+    ScratchAddr& a = g_noalloc_addr[dev];
+    const uint64_t ctx = current_context_id();
+    if (!a.ptr || ctx == 0 || a.ctx != ctx) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_fa_noalloc_scratch);
         if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(flash-attention scratch)");
-        g_noalloc_ptr[dev] = p;
+        a.ptr = p;
+        a.ctx = current_context_id();  // the lookup binds the context if nothing had yet
     }
-    *out = g_noalloc_ptr[dev];
+    *out = a.ptr;
     return HC_OK;
 }
 
@@ -219,9 +257,9 @@ extern "C" int hc_flash_attention_fwd_fused_host_noalloc(const void* h_q, const 
                                                          int dtype, void* stream) {
     if (!t) return fail(HC_ERR_INVALID, "flash_attention host (no-alloc): null tiling");
     if (!h_q || !h_k || !h_v || !h_o) return fail(HC_ERR_INVALID, "flash_attention host (no-alloc): null pointer");
+    int rc = fa_check_tiling(t, t->H, dtype);
+    if (rc) return rc;
     const size_t es = dtype_size(dtype);
-    if (dtype != HC_DTYPE_F32 && dtype != HC_DTYPE_F16 && dtype != HC_DTYPE_BF16)
-        return fail(HC_ERR_UNSUPPORTED, "flash_attention host (no-alloc): dtype %d", dtype);
     const uint64_t bh = static_cast<uint64_t>(t->B) * t->H;
     if (bh == 0 || t->S_q == 0) return ok();
     if (noalloc_chunk_bytes(t, es, 1) > kNoAllocScratchBytes)
@@ -232,7 +270,7 @@ extern "C" int hc_flash_attention_fwd_fused_host_noalloc(const void* h_q, const 
     if (h > bh) h = bh;
     while (h > 1 && noalloc_chunk_bytes(t, es, h) > kNoAllocScratchBytes) --h;
     void* scratch = nullptr;
-    int rc = noalloc_scratch(&scratch);
+    rc = noalloc_scratch(&scratch);
     if (rc) return rc;
     auto align = [](uint64_t v) { return (v + 255) & ~uint64_t(255); };
     const uint64_t q_h = static_cast<uint64_t>(t->S_q) * t->D * es;
@@ -246,24 +284,37 @@ extern "C" int hc_flash_attention_fwd_fused_host_noalloc(const void* h_q, const 
     uint8_t* dO = dv + align(h * v_h);
     float* dl = reinterpret_cast<float*>(dO + align(h * o_h));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // An error after the first copy was queued waits for the stream before returning.
+    auto drain = [&](int status) {
+        cudaStreamSynchronize(s);
+        cudaGetLastError();
+        return status;
+    };
+#define HC_NOALLOC_CHECK(call)                                           \
+    do {                                                                 \
+        cudaError_t e__ = (call);                                        \
+        if (e__ != cudaSuccess) return drain(cuda_fail(e__, #call));     \
+    } while (0)
     for (uint64_t h0 = 0; h0 < bh; h0 += h) {
         const uint64_t hn = (h0 + h <= bh) ? h : (bh - h0);
-        HC_CHECK_CUDA(cudaMemcpyAsync(dq, static_cast<const uint8_t*>(h_q) + h0 * q_h, hn * q_h,
-                                      cudaMemcpyHostToDevice, s));
-        HC_CHECK_CUDA(cudaMemcpyAsync(dk, static_cast<const uint8_t*>(h_k) + h0 * k_h, hn * k_h,
-                                      cudaMemcpyHostToDevice, s));
-        HC_CHECK_CUDA(cudaMemcpyAsync(dv, static_cast<const uint8_t*>(h_v) + h0 * v_h, hn * v_h,
-                                      cudaMemcpyHostToDevice, s));
+        HC_NOALLOC_CHECK(cudaMemcpyAsync(dq, static_cast<const uint8_t*>(h_q) + h0 * q_h, hn * q_h,
+                                         cudaMemcpyHostToDevice, s));
+        HC_NOALLOC_CHECK(cudaMemcpyAsync(dk, static_cast<const uint8_t*>(h_k) + h0 * k_h, hn * k_h,
+                                         cudaMemcpyHostToDevice, s));
+        HC_NOALLOC_CHECK(cudaMemcpyAsync(dv, static_cast<const uint8_t*>(h_v) + h0 * v_h, hn * v_h,
+                                         cudaMemcpyHostToDevice, s));
         flash_attention_fwd_fused_tiling_data tc = *t;
         tc.B = 1;
         tc.H = static_cast<uint32_t>(hn);
         rc = hc_flash_attention_fwd_fused_launch(dq, dk, dv, dO, h_lse ? dl : nullptr, &tc, dtype, s);
-        if (rc) return rc;
-        HC_CHECK_CUDA(cudaMemcpyAsync(static_cast<uint8_t*>(h_o) + h0 * o_h, dO, hn * o_h, cudaMemcpyDeviceToHost, s));
+        if (rc) return drain(rc);
+        HC_NOALLOC_CHECK(
+            cudaMemcpyAsync(static_cast<uint8_t*>(h_o) + h0 * o_h, dO, hn * o_h, cudaMemcpyDeviceToHost, s));
         if (h_lse)
-            HC_CHECK_CUDA(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(h_lse) + h0 * l_h, dl, hn * l_h,
-                                          cudaMemcpyDeviceToHost, s));
+            HC_NOALLOC_CHECK(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(h_lse) + h0 * l_h, dl, hn * l_h,
+                                             cudaMemcpyDeviceToHost, s));
     }
+#undef HC_NOALLOC_CHECK
     HC_CHECK_CUDA(cudaStreamSynchronize(s));
     return hc_check_device_error();
 }

@@ -734,13 +734,9 @@ int launch_tc(const void* q, const void* k, const void* v, void* o, float* lse,
     prm.num_pairs = static_cast<uint32_t>(pairs);
     prm.scale_log2 = t->scale * 1.4426950408889634f;
     prm.causal = t->maskType;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(fa_fwd_tc_kernel<kBF16, HD, HDV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmemBytes));
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fa_fwd_tc_kernel)");
-        attr_set = true;
-    }
+    if (int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(fa_fwd_tc_kernel<kBF16, HD, HDV>), kSmemBytes,
+                                      "fa_fwd_tc_kernel"))
+        return rc;
     uint32_t grid = static_cast<uint32_t>(sm_count());
     if (grid > prm.num_pairs) grid = prm.num_pairs;
     fa_fwd_tc_kernel<kBF16, HD, HDV><<<grid, kThreads, kSmemBytes, stream>>>(tmq, tmk, tmv, prm);
@@ -777,19 +773,29 @@ int launch_simt(const void* q, const void* k, const void* v, void* o, float* lse
 
 using namespace hc;
 
-extern "C" int hc_flash_attention_fwd_fused_gqa_launch(const void* q, const void* k, const void* v, void* o,
-                                                       float* lse, const flash_attention_fwd_fused_tiling_data* t,
-                                                       uint32_t kv_heads, int dtype, void* stream) {
+namespace hc {
+int fa_check_tiling(const flash_attention_fwd_fused_tiling_data* t, uint32_t kv_heads, int dtype) {
     if (!t) return fail(HC_ERR_INVALID, "flash_attention: null tiling");
     if (t->B == 0 || t->H == 0 || t->S_q == 0) return ok();
     if (kv_heads == 0 || t->H % kv_heads != 0)
         return fail(HC_ERR_INVALID, "flash_attention: kv_heads %u must divide H %u", kv_heads, t->H);
-    if (!q || !k || !v || !o) return fail(HC_ERR_INVALID, "flash_attention: null pointer");
     if (t->S_k == 0) return fail(HC_ERR_INVALID, "flash_attention: S_k must be >= 1");
     if (t->D == 0 || t->D_v == 0 || t->D > 256 || t->D_v > 256)
         return fail(HC_ERR_UNSUPPORTED, "flash_attention: D=%u D_v=%u (1..256 supported)", t->D, t->D_v);
     if (t->maskType > 1) return fail(HC_ERR_INVALID, "flash_attention: maskType %u (0 none, 1 causal)", t->maskType);
     if (!std::isfinite(t->scale)) return fail(HC_ERR_INVALID, "flash_attention: scale must be finite");
+    if (dtype != HC_DTYPE_BF16 && dtype != HC_DTYPE_F16 && dtype != HC_DTYPE_F32)
+        return fail(HC_ERR_UNSUPPORTED, "flash_attention: dtype %d not supported (BF16, F16, F32)", dtype);
+    return ok();
+}
+}  // namespace hc
+
+extern "C" int hc_flash_attention_fwd_fused_gqa_launch(const void* q, const void* k, const void* v, void* o,
+                                                       float* lse, const flash_attention_fwd_fused_tiling_data* t,
+                                                       uint32_t kv_heads, int dtype, void* stream) {
+    if (int rc = fa_check_tiling(t, kv_heads, dtype)) return rc;
+    if (t->B == 0 || t->H == 0 || t->S_q == 0) return ok();
+    if (!q || !k || !v || !o) return fail(HC_ERR_INVALID, "flash_attention: null pointer");
     if (fault_hit("launch")) return fail(HC_ERR_INJECTED, "flash_attention: injected launch failure");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool tc_shape = (t->D == 128 || t->D == 64) && (t->D_v == 128 || t->D_v == 64) && t->scale > 0.f &&

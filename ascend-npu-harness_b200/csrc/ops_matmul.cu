@@ -367,13 +367,8 @@ int launch_tc(const void* A, const void* B, const void* bias, void* C, const mat
     prm.tiles_n = (t->N + kBN - 1) / kBN;
     prm.num_tiles = prm.tiles_m * prm.tiles_n;
     prm.k_blocks = (t->K + kBK - 1) / kBK;
-    static bool attr_set[2] = {false, false};
-    if (!attr_set[kBF16]) {
-        cudaError_t e = cudaFuncSetAttribute(mm_tc_kernel<kBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmemBytes));
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(mm_tc_kernel)");
-        attr_set[kBF16] = true;
-    }
+    if (int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(mm_tc_kernel<kBF16>), kSmemBytes, "mm_tc_kernel"))
+        return rc;
     uint32_t grid = static_cast<uint32_t>(sm_count());
     if (grid > prm.num_tiles) grid = prm.num_tiles;
     mm_tc_kernel<kBF16><<<grid, kThreads, kSmemBytes, stream>>>(tma, tmb, prm);

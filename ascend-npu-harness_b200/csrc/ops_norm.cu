@@ -728,13 +728,8 @@ int launch_ln_direct(NormArgs a, cudaStream_t s) {
     a.param_stride = a.H / P / GT * GT * P;  // = H: packs are a multiple of GT
     a.param_floats = 2 * a.param_stride;
     const size_t smem = 128 + static_cast<size_t>(a.param_floats) * 4 + kDirectGroups * 2 * 4 * kGroupWarps * 4;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(ln_direct_kernel<T, KPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(ln_direct_kernel)");
-        attr_set = true;
-    }
+    if (int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(ln_direct_kernel<T, KPL>), smem, "ln_direct_kernel"))
+        return rc;
     const uint64_t groups_needed = (static_cast<uint64_t>(a.rows) + 1) / 2;  // two rows per group at least
     uint64_t grid = (groups_needed + kDirectGroups - 1) / kDirectGroups;
     if (grid > static_cast<uint64_t>(sm_count())) grid = sm_count();
@@ -881,13 +876,9 @@ int launch_rowstream(NormArgs a, cudaStream_t s) {
     }
     a.groups = a.stages - 1 < kGroups ? a.stages - 1 : kGroups;  // keep one stage filling
     const size_t smem = 128 + param_bytes + static_cast<size_t>(a.stages) * a.tile_bytes + bar_bytes;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(rowstream_kernel<T, KIND, G, MODE, KPL>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmemBudget + 1024));
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(rowstream_kernel)");
-        attr_set = true;
-    }
+    if (int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(rowstream_kernel<T, KIND, G, MODE, KPL>),
+                                      kSmemBudget + 1024, "rowstream_kernel"))
+        return rc;
     const uint64_t tiles = (a.rows + a.tile_rows - 1) / a.tile_rows;
     const uint64_t grid = tiles < static_cast<uint64_t>(sm_count()) ? tiles : static_cast<uint64_t>(sm_count());
     rowstream_kernel<T, KIND, G, MODE, KPL><<<static_cast<unsigned>(grid), kThreads, smem, s>>>(a);
@@ -932,9 +923,9 @@ int launch_rownorm(NormArgs a, void* stream) {
     size_t smem = static_cast<size_t>(a.H) * sizeof(float);
     if (smem > 200 * 1024) return fail(HC_ERR_UNSUPPORTED, "row length %u too long for the scalar row kernel", a.H);
     if (smem > 48 * 1024) {
-        if (cudaFuncSetAttribute(rownorm_scalar_kernel<T, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(smem)) != cudaSuccess)
-            return cuda_fail(cudaGetLastError(), "cudaFuncSetAttribute(rownorm_scalar)");
+        if (int rc = set_max_dynamic_smem(reinterpret_cast<const void*>(rownorm_scalar_kernel<T, KIND>), smem,
+                                          "rownorm_scalar_kernel"))
+            return rc;
     }
     const uint64_t cap =
         static_cast<uint64_t>(resident_blocks(reinterpret_cast<const void*>(rownorm_scalar_kernel<T, KIND>), 256, smem));

@@ -394,16 +394,10 @@ bool launch_transpose16_tma(const void* src, void* dst, uint32_t batch, uint32_t
     TileMap map;
     if (!make_tile_map(map, batch, R, C, kTmaRows, kTmaCols)) return false;
     static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-        register_error_word(read_transpose_error_word);
-        attr_err = cudaFuncSetAttribute(transpose16_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(kTmaSmemBytes));
-    });
-    if (attr_err != cudaSuccess) {
-        *status = cuda_fail(attr_err, "cudaFuncSetAttribute(transpose16_tma_kernel)");
-        return true;
-    }
+    std::call_once(once, [] { register_error_word(read_transpose_error_word); });
+    *status = set_max_dynamic_smem(reinterpret_cast<const void*>(transpose16_tma_kernel), kTmaSmemBytes,
+                                   "transpose16_tma_kernel");
+    if (*status != HC_OK) return true;
     CUtensorMap tm;
     const uint64_t dims[3] = {C, R, batch};
     const uint64_t strides[2] = {static_cast<uint64_t>(C) * 2, static_cast<uint64_t>(R) * C * 2};

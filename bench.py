@@ -2,21 +2,27 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extras]
 
-One step = one flash_attention_fwd_fused forward over the benchmarked configuration on every GPU:
+One step = one flash_attention_fwd_fused forward over the benchmarked configuration:
 Q, K, V bf16 [B=16, H=32, S=8192, D=128], causal, scale 1/sqrt(128), O bf16 + lse fp32.
-Weak scaling: each rank owns a full 16x32-head shard of a global batch of 16*N (the work shards
-over batch x heads with no exchange, so there is no collective on the data path).  Time is
-measured with CUDA events on the launching stream between barriers, max over ranks; rank 0 prints
-one JSON line.  Inputs (3.2 GB per GPU) are larger than the 126 MB L2.
+Strong scaling: the 16 x 32 = 512 (batch, head) pairs of the one fixed problem are split over the
+N ranks (one process per GPU, torchrun), 512/N heads each; the work shards over batch x heads with
+no exchange, so there is no collective on the data path.  Time is measured with CUDA events on the
+launching stream between barriers, max over ranks; `value` is the whole problem's FLOPs divided by
+that time.  Rank 0 prints one JSON line.  Inputs (3.2 GB at N=1) are larger than the 126 MB L2.
 
 Extra keys of the JSON line:
   roofline     the flash-attention kernel against the measured dense bf16 peak
+  accuracy     the headline output of the timed launches checked after timing: sampled heads of
+               every rank against a torch fp32 reference on the device (max-abs / max-rel)
   e2e          the same metric through the C ABI's host-buffer entry point
                (hc_flash_attention_fwd_fused_host: pinned H2D copies, kernel, D2H copies, per step)
   cpu_baseline the reference golden (compiled from the reference sources into oracle/_ref) on the
                host cores, on a bounded sample (rank 0, N=1 only)
-  ops          the other benchmarked configurations (non-causal attention, matmul_bias, layer_norm,
-               rms_norm_rope_fused, elementwise_add) with their roofline fractions
+  weak         (N > 1) every rank running the full 512-head problem: the per-GPU-constant figure
+  ops          the other benchmarked configurations, each split over the ranks like the headline,
+               as {value, unit, frac, ms, max_abs, max_rel, pass}; the accuracy columns come from
+               a sampled check of that op's output in the same run (torch fp32 reference on the
+               device; bit-exact ops compare bits)
   clocks       SM clocks and throttle reasons sampled with nvidia-smi during the timed region
 
 --impl reference times the reference's own CPU implementation of the path (oracle/_ref, all host
@@ -210,11 +216,56 @@ def whole_job_rate(units_per_rank: float, world: int, ms_max: float) -> float:
     return world * units_per_rank / (ms_max * 1e-3)
 
 
+def shard_range(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Strong scaling: rank `rank`'s contiguous share (start, count) of `total` independent units
+    (attention heads, matrix rows, sequence positions, elements).  Shares differ by at most one
+    unit and together cover every unit exactly once."""
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, base + (1 if rank < extra else 0)
+
+
+def fixed_job_rate(total_units: float, ms_max: float) -> float:
+    """Strong scaling: the one fixed problem's units divided by the slowest rank's time."""
+    return total_units / (ms_max * 1e-3)
+
+
+def rel_err(expected, actual):
+    """Element-wise relative error as the harness's accuracy::CompareArrays defines it
+    (include/harness/accuracy.hpp:78-83): |e - a| / |e|, or / |a| when |e| <= 1e-12."""
+    import torch
+
+    e, a = expected.double(), actual.double()
+    d = (e - a).abs()
+    den = torch.where(e.abs() > 1e-12, e.abs(), a.abs())
+    return torch.where(den > 1e-12, d / den.clamp_min(1e-300), torch.zeros_like(d))
+
+
+def accuracy(expected, actual, abs_tol: float, rel_tol: float) -> dict:
+    """Max-abs and max-rel error over all compared elements, and the CompareArrays verdict: an element
+    fails only when it exceeds both tolerances."""
+    d = (expected.double() - actual.double()).abs()
+    r = rel_err(expected, actual)
+    fails = int(((d > abs_tol) & (r > rel_tol)).sum().item())
+    return {"max_abs": float(d.max().item()) if d.numel() else 0.0,
+            "max_rel": float(r.max().item()) if r.numel() else 0.0, "pass": fails == 0}
+
+
+def sig(x, n: int = 4):
+    """Rounds floats to `n` significant digits (keeps the JSON line short)."""
+    if isinstance(x, float) and math.isfinite(x) and x != 0.0:
+        return round(x, n - 1 - int(math.floor(math.log10(abs(x)))))
+    if isinstance(x, dict):
+        return {k: sig(v, n) for k, v in x.items()}
+    return x
+
+
 # ------------------------------------------------------------------------------------------------
 # timing helpers
 # ------------------------------------------------------------------------------------------------
-def time_launches(fn, steps: int, warmup: int, d: Dist, flush=None, spin: bool = True):
-    """Returns (ms per launch averaged over `steps`, max over ranks).
+def time_launches(fn, steps: int, warmup: int, d: Dist, flush=None, spin: bool = True, local: bool = False):
+    """Returns ms per launch averaged over `steps`: the max over ranks, or this rank's own figure
+    with `local` (the barriers are the same either way).
 
     Without `flush` (every workload here reads more than the 126 MB L2 per launch) the `steps`
     launches run back to back between one pair of events; a spin kernel queued first keeps the
@@ -249,7 +300,7 @@ def time_launches(fn, steps: int, warmup: int, d: Dist, flush=None, spin: bool =
         torch.cuda.synchronize()
         ms = sum(s.elapsed_time(e) for s, e in evs) / steps
     d.barrier()
-    return d.max(ms)
+    return ms if local else d.max(ms)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -314,8 +365,63 @@ def run_reference_arm(args):
 
 
 # ------------------------------------------------------------------------------------------------
+# torch fp32/fp64 references for the in-run accuracy checks (device-side; the oracle is not used)
+# ------------------------------------------------------------------------------------------------
+def fa_reference(q, k, v, causal: bool, scale: float):
+    """O and lse of one head ([S, D] tensors) in float64 on the device: softmax(q k^T * scale) v."""
+    import torch
+
+    qd, kd, vd = q.double(), k.double(), v.double()
+    s = (qd @ kd.transpose(0, 1)) * scale
+    if causal:
+        s = s.masked_fill(torch.ones_like(s, dtype=torch.bool).triu(1), float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    o = torch.softmax(s, dim=-1) @ vd
+    return o, lse
+
+
+def check_fa_heads(q, k, v, o, lse, causal: bool, n_sample: int = 4) -> dict:
+    """Sampled heads of this rank's shard ([1, h, S, D]) against fa_reference: O max-abs 2e-2, lse 2e-3."""
+    import torch
+
+    h = q.shape[1]
+    heads = sorted({0, h - 1, *[int(i) for i in torch.linspace(0, h - 1, n_sample).round().tolist()]})
+    scale = 1.0 / math.sqrt(q.shape[-1])
+    worst = {"max_abs": 0.0, "max_rel": 0.0, "pass": True, "lse_max_abs": 0.0}
+    for i in heads:
+        o_ref, l_ref = fa_reference(q[0, i], k[0, i], v[0, i], causal, scale)
+        acc = accuracy(o_ref, o[0, i], 2e-2, 0.0)
+        lerr = float((l_ref - lse[0, i].double()).abs().max().item())
+        worst["max_abs"] = max(worst["max_abs"], acc["max_abs"])
+        worst["max_rel"] = max(worst["max_rel"], acc["max_rel"])
+        worst["lse_max_abs"] = max(worst["lse_max_abs"], lerr)
+        worst["pass"] = worst["pass"] and acc["pass"] and lerr <= 2e-3
+    worst["heads_checked"] = len(heads)
+    return worst
+
+
+def merge_acc(d: "Dist", acc: dict) -> dict:
+    """Worst accuracy over the ranks (max of the errors, AND of the verdicts)."""
+    out = dict(acc)
+    for key in ("max_abs", "max_rel", "lse_max_abs"):
+        if key in acc:
+            out[key] = d.max(acc[key])
+    out["pass"] = d.max(0.0 if acc["pass"] else 1.0) == 0.0
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
 # our arm
 # ------------------------------------------------------------------------------------------------
+def fa_inputs(dev, heads: int, seed_base: int):
+    """Q, K, V bf16 [1, heads, S, D] ~ N(0,1) from torch's seeded CUDA generator."""
+    import torch
+
+    gens = [torch.Generator(device=dev).manual_seed(s + seed_base) for s in (0, 1, 2)]
+    return [torch.randn((1, heads, FA_S, FA_D), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+            for g in gens]
+
+
 def run_ours(args):
     import ctypes
 
@@ -331,14 +437,13 @@ def run_ours(args):
     lib = hc.load()  # raises if the CUDA library is missing: there is no CPU fallback
     peaks, peak_src = load_peaks()
     n = d.world
-    fa_b = args.fa_batch
+    total_heads = args.fa_batch * FA_H
+    h0, hn = shard_range(total_heads, n, d.rank)
 
-    # ---------------- headline: causal flash attention -----------------------------------------
-    gens = [torch.Generator(device=dev).manual_seed(s + 3 * d.rank) for s in (0, 1, 2)]
-    q, k, v = (torch.randn((fa_b, FA_H, FA_S, FA_D), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
-               for g in gens)
+    # ---------------- headline: causal flash attention, the fixed problem split over the ranks -------
+    q, k, v = fa_inputs(dev, hn, 3 * d.rank)
     o = torch.empty_like(q)
-    lse = torch.empty((fa_b, FA_H, FA_S), dtype=torch.float32, device=dev)
+    lse = torch.empty((1, hn, FA_S), dtype=torch.float32, device=dev)
     step = lambda: hc.flash_attention_fwd(q, k, v, True, out=o, lse=lse)  # noqa: E731
     step()
     torch.cuda.synchronize()
@@ -369,14 +474,16 @@ def run_ours(args):
     ms_local = s_ev.elapsed_time(e_ev) / args.steps
     hc.check_device_error()
     ms = d.max(ms_local)
-    flops_rank = fa_flops(fa_b, FA_H, FA_S, FA_S, FA_D, True)
-    value = whole_job_rate(flops_rank, n, ms) / 1e12
+    flops_total = fa_flops(1, total_heads, FA_S, FA_S, FA_D, True)
+    flops_rank = fa_flops(1, hn, FA_S, FA_S, FA_D, True)
+    value = fixed_job_rate(flops_total, ms) / 1e12
     achieved = flops_rank / (ms_local * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops"],
-                "peak_source": f"{peak_src} bf16_tflops (burst: the kernel is timed alone)",
+                "peak_source": f"{peak_src} bf16_tflops (burst)",
                 "traffic": profile_traffic("flash_attention_fwd_causal"),
                 "algorithmic_flops_per_launch": flops_rank}
+    acc = merge_acc(d, check_fa_heads(q, k, v, o, lse, True))
 
     # ---------------- optional: the sharded outputs gathered onto every rank (after timing) -----------
     gather = None
@@ -390,8 +497,7 @@ def run_ours(args):
         torch.cuda.synchronize()
         g_ms = d.max(g0.elapsed_time(g1))
         own_ok = 1.0 - d.max(0.0 if torch.equal(full[d.rank], o) else 1.0)  # 1 only if every rank's slice is its own O
-        gather = {"what": f"O [{fa_b}, {FA_H}, {FA_S}, {FA_D}] bf16 of every rank onto every rank (NCCL all-gather)",
-                  "bytes_per_rank": o.numel() * 2, "gathered_bytes": full.numel() * 2, "ms": g_ms,
+        gather = {"bytes_per_rank": o.numel() * 2, "ms": g_ms,
                   "gb_per_s_in_per_rank": (n - 1) * o.numel() * 2 / (g_ms * 1e-3) / 1e9, "own_slices_equal": own_ok == 1.0}
         del full
     del o
@@ -401,8 +507,8 @@ def run_ours(args):
     if not args.no_e2e:
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
         ho = torch.empty_like(hq).pin_memory()
-        hl = torch.empty((fa_b, FA_H, FA_S), dtype=torch.float32).pin_memory()
-        t = hc.FlashAttentionFwdFusedTiling(fa_b, FA_H, FA_S, FA_S, FA_D, FA_D, 1.0 / math.sqrt(FA_D), 1)
+        hl = torch.empty((1, hn, FA_S), dtype=torch.float32).pin_memory()
+        t = hc.FlashAttentionFwdFusedTiling(1, hn, FA_S, FA_S, FA_D, FA_D, 1.0 / math.sqrt(FA_D), 1)
         ws = ctypes.c_size_t()
         hc.check(lib.hc_flash_attention_fwd_fused_host_workspace_size(ctypes.byref(t), hc.DT_BF16, ctypes.byref(ws)))
         work = torch.empty(ws.value, dtype=torch.uint8, device=dev)
@@ -415,14 +521,27 @@ def run_ours(args):
 
         e2e_steps = max(2, min(args.steps, 5))
         e2e_ms = time_launches(e2e_step, e2e_steps, 1, d, spin=False)
-        h2d = 3 * q.numel() * 2
-        d2h = ho.numel() * 2 + hl.numel() * 4
-        e2e = {"value": n * flops_rank / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+        h2d = 3 * total_heads * FA_S * FA_D * 2
+        d2h = total_heads * FA_S * (FA_D * 2 + 4)
+        e2e = {"value": fixed_job_rate(flops_total, e2e_ms) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "api": "hc_flash_attention_fwd_fused_host (pinned host buffers, chunked copies overlapped with the kernel)"}
+               "api": "hc_flash_attention_fwd_fused_host (pinned host buffers; bytes summed over ranks)"}
         del hq, hk, hv, ho, hl, work
     del q, k, v, lse
     torch.cuda.empty_cache()
+
+    # ---------------- weak scaling (N > 1): every rank runs the whole 512-head problem ---------------
+    weak = None
+    if n > 1 and not args.no_weak:
+        q, k, v = fa_inputs(dev, total_heads, 3 * d.rank)
+        o = torch.empty_like(q)
+        lse = torch.empty((1, total_heads, FA_S), dtype=torch.float32, device=dev)
+        w_ms = time_launches(lambda: hc.flash_attention_fwd(q, k, v, True, out=o, lse=lse), max(3, args.steps // 4),
+                             args.warmup, d)
+        weak = {"value": whole_job_rate(flops_total, n, w_ms) / 1e12, "unit": "TFLOP/s", "ms_per_step": w_ms,
+                "per_gpu_heads": total_heads}
+        del q, k, v, o, lse
+        torch.cuda.empty_cache()
 
     # ---------------- the other benchmarked configurations ------------------------------------
     ops = {} if args.no_extras else run_extras(hc, d, dev, peaks, args)
@@ -437,27 +556,30 @@ def run_ours(args):
     if d.rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": n, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: Q,K,V ~ N(0,1) from torch's seeded CUDA generator (seeds 0/1/2, +3 per rank), bf16",
-            "config": {"workload": f"flash_attention_fwd_fused causal bf16 B{fa_b} H32 S8192 D128 per GPU (O bf16 + lse fp32)",
-                       "global_batch": fa_b * n, "seq_len": FA_S, "heads": FA_H, "head_dim": FA_D, "causal": True,
-                       "parallelism": f"dp{n}: batch x heads sharded, no collective",
-                       "l2": "inputs 3.2 GB per GPU > 126 MB L2; no flush needed"},
+            "data": "synthetic: Q,K,V ~ N(0,1), torch CUDA generator seeds 0/1/2 (+3 per rank), bf16",
+            "config": {"workload": f"flash_attention_fwd_fused causal bf16 B{args.fa_batch} H32 S8192 D128, "
+                                   f"O bf16 + lse fp32; {total_heads} heads split over {n} GPU(s)",
+                       "global_batch": args.fa_batch, "seq_len": FA_S, "heads": FA_H, "head_dim": FA_D,
+                       "causal": True, "parallelism": f"dp{n}: batch x heads sharded, no collective",
+                       "l2": "inputs > 126 MB L2 per GPU; no flush"},
             "gpu_launches": args.steps,
-            "roofline": roofline, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "ops": ops,
-            **({"gather": gather} if gather else {}),
-            "device": torch.cuda.get_device_name(dev),
+            "roofline": sig(roofline), "accuracy": sig(acc), "e2e": sig(e2e), "cpu_baseline": sig(cpu),
+            "clocks": clocks,
+            **({"weak": sig(weak)} if weak else {}),
+            **({"gather": sig(gather)} if gather else {}),
+            "ops": {k_: sig(v_) for k_, v_ in ops.items()},
         }
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line, separators=(",", ":")), flush=True)
     d.close()
 
 
 EXTRA_OPS = ("flash_attention_fwd_noncausal", "matmul_bias", "layer_norm", "rms_norm_rope_fused", "elementwise_add",
              "axpy_scalar_affine", "broadcast_binary", "activation_gelu_silu", "reduce_sum_lastdim", "transpose_2d_4d")
 # The last five ops have no configuration of their own in the reference's benchmark list; they are
-# timed on sized analogs of the layer_norm shape (134 MB of 16-bit input per launch), stated in
-# each entry's "config".
+# timed on sized analogs of the layer_norm shape (134 MB of 16-bit input per launch); the shapes
+# are listed in the design notes.
 ANALOG_OPS = EXTRA_OPS[5:]
 
 
@@ -472,74 +594,88 @@ def settle():
 
 
 def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
-    """The other benchmarked configurations, each timed alone (W=3, 20 launches)."""
+    """The other benchmarked configurations, each split over the ranks like the headline and timed
+    alone (W=3, 20 launches; 5 for attention).  Each entry: whole-job rate (total work / slowest
+    rank's time), the kernel's roofline fraction on its shard, and the accuracy of that output
+    against a device-side torch reference (sampled where the full check would dominate the run)."""
     import torch
 
     out = {}
     if not want:
         return out
     steps, warm = 20, 3
-    # The bandwidth workloads below each read more than the 126 MB L2 per launch (layer_norm
-    # 134 MB, rms_norm_rope 268 MB, elementwise_add 134 MB), so they run back to back without an
-    # L2 flush; consecutive launches alternate between two independent buffer sets, so a launch
-    # can neither re-read the previous launch's inputs nor rewrite its still-dirty outputs in L2.
+    n, r = d.world, d.rank
+    # The bandwidth workloads below run back to back without an L2 flush; consecutive launches cycle
+    # through independent buffer sets whose total exceeds twice the 126 MB L2 (two sets at N=1, where
+    # each launch alone reads more than L2; more at N=8, where a 17-67 MB shard would fit), so a
+    # launch can neither re-read a recent launch's inputs nor rewrite its still-dirty outputs in L2.
     hbm = peaks["hbm_gbs"]
     flip = [0]
 
     def alternate(sets):
+        """Cycles through the buffer sets; flip[0] is the index of the set used last."""
         def nxt():
-            flip[0] ^= 1
+            flip[0] = (flip[0] + 1) % len(sets)
             return sets[flip[0]]
         return nxt
-    g = torch.Generator(device=dev).manual_seed(0)
 
-    def bw_entry(name, bytes_, ms, launches=1):
-        gbs = bytes_ / (ms * 1e-3) / 1e9
-        out[name] = {"value": d.world * gbs, "unit": "GB/s", "per_gpu": gbs, "ms": ms,
-                     "timing": f"after a 1 s idle pause, {steps} back-to-back launches alternating two buffer sets, "
-                               "no L2 flush (each reads > 126 MB)",
-                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                                  "algorithmic_bytes_per_launch": bytes_, "traffic": profile_traffic(name)}}
+    def rotation(make_set, set_bytes):
+        """Enough independent buffer sets that one cycle moves more than twice the 126 MB L2 (two at
+        least): at N = 8 a single shard fits in L2, and back-to-back launches would otherwise re-read it."""
+        count = max(2, min(32, math.ceil(2.2 * 126e6 / max(set_bytes, 1))))
+        return [make_set() for _ in range(count)]
+    g = torch.Generator(device=dev).manual_seed(100 + r)
+
+    def entry(name, total_units, rank_units, unit_bytes_or_flops, ms_local, acc, bound):
+        ms = d.max(ms_local)
+        per = rank_units * unit_bytes_or_flops / (ms_local * 1e-3)
+        acc = merge_acc(d, acc)
+        if bound == "hbm":
+            job = total_units * unit_bytes_or_flops / (ms * 1e-3) / 1e9
+            e = {"value": job, "unit": "GB/s", "frac": per / 1e9 / hbm}
+        else:
+            job = total_units * unit_bytes_or_flops / (ms * 1e-3) / 1e12
+            e = {"value": job, "unit": "TFLOP/s", "frac": per / 1e12 / peaks["bf16_tflops"]}
+        e.update({"ms": ms, "max_abs": acc["max_abs"], "max_rel": acc["max_rel"], "pass": acc["pass"]})
+        out[name] = e
 
     if "flash_attention_fwd_noncausal" in want:  # same shapes as the headline, no mask
-        q, k, v = (torch.randn((FA_B, FA_H, FA_S, FA_D), generator=g, device=dev).to(torch.bfloat16) for _ in range(3))
+        total = args.fa_batch * FA_H
+        _, hn = shard_range(total, n, r)
+        q, k, v = fa_inputs(dev, hn, 50 + 3 * r)
         o = torch.empty_like(q)
-        lse = torch.empty((FA_B, FA_H, FA_S), dtype=torch.float32, device=dev)
+        lse = torch.empty((1, hn, FA_S), dtype=torch.float32, device=dev)
         settle()
-        ms = time_launches(lambda: hc.flash_attention_fwd(q, k, v, False, out=o, lse=lse), 5, warm, d)
-        fl = fa_flops(FA_B, FA_H, FA_S, FA_S, FA_D, False)
-        tf = fl / (ms * 1e-3) / 1e12
-        out["flash_attention_fwd_noncausal"] = {
-            "value": d.world * tf, "unit": "TFLOP/s", "per_gpu": tf, "ms": ms,
-            "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": tf / peaks["bf16_tflops"], "algorithmic_flops_per_launch": fl}}
+        ms = time_launches(lambda: hc.flash_attention_fwd(q, k, v, False, out=o, lse=lse), 5, warm, d, local=True)
+        acc = check_fa_heads(q, k, v, o, lse, False, n_sample=2)
+        entry("flash_attention_fwd_noncausal", total, hn, fa_flops(1, 1, FA_S, FA_S, FA_D, False), ms, acc, "tensor")
         del q, k, v, o, lse
 
-    if "matmul_bias" in want:  # 8192^3 bf16, A, B ~ N(0,1)/sqrt(K), bias ~ N(0, 0.1)
+    if "matmul_bias" in want:  # 8192^3 bf16, M rows split over the ranks, B replicated
         M = K = N = 8192
-        A = (torch.randn((M, K), generator=g, device=dev) / math.sqrt(K)).to(torch.bfloat16)
+        _, mn = shard_range(M, n, r)
+        A = (torch.randn((mn, K), generator=g, device=dev) / math.sqrt(K)).to(torch.bfloat16)
         B = (torch.randn((K, N), generator=g, device=dev) / math.sqrt(K)).to(torch.bfloat16)
         bias = (torch.randn((N,), generator=g, device=dev) * 0.1).to(torch.bfloat16)
-        C = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+        C = torch.empty((mn, N), dtype=torch.bfloat16, device=dev)
         settle()
-        ms = time_launches(lambda: hc.matmul_bias(A, B, bias, out=C), steps, warm, d)
-        fl = 2.0 * M * N * K
-        tf = fl / (ms * 1e-3) / 1e12
-        out["matmul_bias"] = {"value": d.world * tf, "unit": "TFLOP/s", "per_gpu": tf, "ms": ms,
-                              "roofline": {"bound": "tensor", "achieved": tf, "peak": peaks["bf16_tflops"],
-                                           "unit": "TFLOP/s", "frac": tf / peaks["bf16_tflops"],
-                                           "algorithmic_flops_per_launch": fl,
-                                           "algorithmic_bytes_per_launch": 3 * M * N * 2 + N * 2,
-                                           "traffic": profile_traffic("matmul_bias")}}
-        del A, B, bias, C
+        ms = time_launches(lambda: hc.matmul_bias(A, B, bias, out=C), steps, warm, d, local=True)
+        rows = torch.unique(torch.cat([torch.tensor([0, mn - 1]), torch.randint(0, mn, (62,))])).to(dev)
+        ref = A[rows].double() @ B.double() + bias.double()
+        acc = accuracy(ref, C[rows], 0.0, 0.0)
+        acc["pass"] = float((ref - C[rows].double()).abs().max() / ref.abs().max()) <= 1e-2  # rel-err <= 1e-2
+        entry("matmul_bias", M, mn, 2.0 * N * K, ms, acc, "tensor")
+        del A, B, bias, C, ref
 
-    if "layer_norm" in want:  # [16384, 4096] bf16, fp32 gamma/beta
-        gamma = torch.rand((4096,), generator=g, device=dev) + 0.5
-        beta = torch.rand((4096,), generator=g, device=dev) * 0.2 - 0.1
-        sets = []
-        for _ in range(2):
-            x = torch.randn((16384, 4096), generator=g, device=dev).to(torch.bfloat16)
-            sets.append((x, torch.empty_like(x)))
+    if "layer_norm" in want:  # [16384, 4096] bf16, fp32 gamma/beta, rows split over the ranks
+        R, H = 16384, 4096
+        _, rn = shard_range(R, n, r)
+        gamma = torch.rand((H,), generator=g, device=dev) + 0.5
+        beta = torch.rand((H,), generator=g, device=dev) * 0.2 - 0.1
+        def ln_set():
+            x = torch.randn((rn, H), generator=g, device=dev).to(torch.bfloat16)
+            return x, torch.empty_like(x)
+        sets = rotation(ln_set, 2 * rn * H * 2)
         nxt = alternate(sets)
 
         def ln_step():
@@ -547,97 +683,125 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
             hc.layer_norm(xx, gamma, beta, 1e-5, y=yy)
 
         settle()
-        ms = time_launches(ln_step, steps, warm, d)
-        bw_entry("layer_norm", 2 * x.numel() * 2 + 2 * 4096 * 4, ms)
-        del x, sets
+        ms = time_launches(ln_step, steps, warm, d, local=True)
+        x, y = sets[flip[0]]
+        rows = torch.linspace(0, rn - 1, 64, device=dev).long()
+        xd = x[rows].double()
+        mean = xd.mean(-1, keepdim=True)
+        var = ((xd - mean) ** 2).mean(-1, keepdim=True)
+        ref = (xd - mean) / torch.sqrt(var + 1e-5) * gamma.double() + beta.double()
+        acc = accuracy(ref, y[rows], 1e-2, 2.0 ** -8)
+        entry("layer_norm", R, rn, 2 * H * 2 + 2 * H * 4 / rn, ms, acc, "hbm")
+        del x, y, sets
 
-    if "rms_norm_rope_fused" in want:  # [8, 4096, 32, 128] bf16, rotate-half, fp32 cos/sin [4096, 64]
-        w = torch.rand((128,), generator=g, device=dev) + 0.5
-        pos = torch.arange(4096, device=dev, dtype=torch.float32)[:, None]
-        inv = 1.0 / (10000.0 ** (torch.arange(64, device=dev, dtype=torch.float32) * 2 / 128))
-        cos, sin = torch.cos(pos * inv).contiguous(), torch.sin(pos * inv).contiguous()
-        sets = []
-        for _ in range(2):
-            x = torch.randn((8, 4096, 32, 128), generator=g, device=dev).to(torch.bfloat16)
-            sets.append((x, torch.empty_like(x)))
+    if "rms_norm_rope_fused" in want:  # [8, 4096, 32, 128] bf16, rotate-half, positions split over the ranks
+        Bb, S, Hh, D = 8, 4096, 32, 128
+        s0, sn = shard_range(S, n, r)
+        w = torch.rand((D,), generator=g, device=dev) + 0.5
+        pos = torch.arange(S, device=dev, dtype=torch.float32)[:, None]
+        inv = 1.0 / (10000.0 ** (torch.arange(D // 2, device=dev, dtype=torch.float32) * 2 / D))
+        cos_all, sin_all = torch.cos(pos * inv), torch.sin(pos * inv)
+        cos, sin = cos_all[s0:s0 + sn].contiguous(), sin_all[s0:s0 + sn].contiguous()
+        def rms_set():
+            x = torch.randn((Bb, sn, Hh, D), generator=g, device=dev).to(torch.bfloat16)
+            return x, torch.empty_like(x)
+        sets = rotation(rms_set, 2 * Bb * sn * Hh * D * 2)
         nxt = alternate(sets)
 
         def rms_step():
             xx, yy = nxt()
-            hc.rms_norm_rope_fused(xx, w, cos, sin, 128, 1e-6, heads=32, rope_style=1, out=yy)
+            hc.rms_norm_rope_fused(xx, w, cos, sin, D, 1e-6, heads=Hh, rope_style=1, out=yy)
 
         settle()
-        ms = time_launches(rms_step, steps, warm, d)
-        bw_entry("rms_norm_rope_fused", 2 * x.numel() * 2 + 128 * 4 + 2 * cos.numel() * 4, ms)
-        del x, sets
+        ms = time_launches(rms_step, steps, warm, d, local=True)
+        x, y = sets[flip[0]]
+        xs = x[:, :: max(1, sn // 16)].double()  # 16 positions of every batch, all heads
+        ys = y[:, :: max(1, sn // 16)]
+        cs, ss = cos[:: max(1, sn // 16)].double()[None, :, None], sin[:: max(1, sn // 16)].double()[None, :, None]
+        xn = xs / torch.sqrt((xs * xs).mean(-1, keepdim=True) + 1e-6) * w.double()
+        lo, hi = xn[..., : D // 2], xn[..., D // 2:]
+        ref = torch.cat([lo * cs - hi * ss, hi * cs + lo * ss], dim=-1)
+        acc = accuracy(ref, ys, 2e-2, 2.0 ** -8)
+        # per (position, head) row: x in and out, plus its share of the position's cos/sin row
+        entry("rms_norm_rope_fused", Bb * S * Hh, Bb * sn * Hh, 2 * D * 2 + 2 * (D // 2) * 4 / (Bb * Hh), ms, acc, "hbm")
+        del x, y, sets
 
-    if "elementwise_add" in want:  # fp16 [4096, 8192], U[-1, 1]
-        sets = []
-        for _ in range(2):
-            a = (torch.rand((4096, 8192), generator=g, device=dev) * 2 - 1).to(torch.float16)
-            b = (torch.rand((4096, 8192), generator=g, device=dev) * 2 - 1).to(torch.float16)
-            sets.append((a, b, torch.empty_like(a)))
+    if "elementwise_add" in want:  # fp16 [4096, 8192], U[-1, 1], flat range split over the ranks
+        total = 4096 * 8192
+        _, en = shard_range(total, n, r)
+        def add_set():
+            a = (torch.rand((en,), generator=g, device=dev) * 2 - 1).to(torch.float16)
+            b = (torch.rand((en,), generator=g, device=dev) * 2 - 1).to(torch.float16)
+            return a, b, torch.empty_like(a)
+        sets = rotation(add_set, 3 * en * 2)
         nxt = alternate(sets)
         settle()
-        ms = time_launches(lambda: hc.elementwise_add(*nxt()), steps, warm, d)
-        bw_entry("elementwise_add", 3 * a.numel() * 2, ms)
-        del a, b, sets
+        ms = time_launches(lambda: hc.elementwise_add(*nxt()), steps, warm, d, local=True)
+        a, b, z = sets[flip[0]]
+        ref = a + b  # torch's fp16 add: fp32 sum, one round-to-nearest-even (the golden's arithmetic)
+        acc = accuracy(ref, z, 0.0, 0.0)
+        acc["pass"] = bool(torch.equal(ref.view(torch.int16), z.view(torch.int16)))  # bit-exact
+        entry("elementwise_add", total, en, 3 * 2, ms, acc, "hbm")
+        del a, b, z, sets
     if any(op in want for op in ANALOG_OPS):
-        out.update(run_analogs(hc, d, dev, peaks, want, steps, warm, alternate))
+        run_analogs(hc, d, dev, want, steps, warm, alternate, rotation, entry, flip)
     torch.cuda.empty_cache()
     return out
 
 
-def run_analogs(hc, d: Dist, dev, peaks, want, steps, warm, alternate) -> dict:
-    """Sized analogs for the ops without a configuration of their own: bf16, 134 MB of input."""
+def run_analogs(hc, d: Dist, dev, want, steps, warm, alternate, rotation, entry, flip) -> None:
+    """Sized analogs for the ops without a configuration of their own: bf16, 134 MB of input at
+    N=1 (the layer_norm shape), rows split over the ranks."""
     import torch
 
-    out = {}
-    g = torch.Generator(device=dev).manual_seed(7)
-    hbm = peaks["hbm_gbs"]
+    g = torch.Generator(device=dev).manual_seed(7 + d.rank)
     R, K = 16384, 4096  # the layer_norm shape
+    _, rn = shard_range(R, d.world, d.rank)
 
     def rnd(*shape):
         return torch.randn(shape, generator=g, device=dev).to(torch.bfloat16)
 
-    def entry(name, config, bytes_, make_set, run):
-        sets = [make_set() for _ in range(2)]
+    def timed(make_set, run, set_bytes):
+        sets = rotation(make_set, set_bytes)
         nxt = alternate(sets)
         settle()
-        ms = time_launches(lambda: run(*nxt()), steps, warm, d)
-        gbs = bytes_ / (ms * 1e-3) / 1e9
-        out[name] = {"value": d.world * gbs, "unit": "GB/s", "per_gpu": gbs, "ms": ms, "config": config,
-                     "timing": f"after a 1 s idle pause, {steps} back-to-back launches alternating two buffer sets, no L2 flush",
-                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
-                                  "algorithmic_bytes_per_launch": bytes_, "traffic": profile_traffic(name)}}
+        ms = time_launches(lambda: run(*nxt()), steps, warm, d, local=True)
+        return ms, sets[flip[0]]
 
-    n = R * K
-    if "axpy_scalar_affine" in want:
-        entry("axpy_scalar_affine", f"analog: bf16 [{R}, {K}], y = 0.5 x - 1", 2 * n * 2,
-              lambda: (rnd(R, K), torch.empty((R, K), dtype=torch.bfloat16, device=dev)),
-              lambda x, y: hc.axpy_scalar_affine(x, 0.5, -1.0, y=y))
-    if "broadcast_binary" in want:
+    def exact(ref, got):
+        acc = accuracy(ref.float(), got.float(), 0.0, 0.0)
+        acc["pass"] = bool(torch.equal(ref.view(torch.int16), got.view(torch.int16)))
+        return acc
+
+    if "axpy_scalar_affine" in want:  # y = 0.5 x - 1 in fp32, one rounding to bf16 (bit-exact)
+        ms, (x, y) = timed(lambda: (rnd(rn, K), torch.empty((rn, K), dtype=torch.bfloat16, device=dev)),
+                           lambda x, y: hc.axpy_scalar_affine(x, 0.5, -1.0, y=y), 2 * rn * K * 2)
+        entry("axpy_scalar_affine", R, rn, 2 * K * 2, ms, exact((x.float() * 0.5 + -1.0).to(torch.bfloat16), y), "hbm")
+    if "broadcast_binary" in want:  # x [16, 256, 128, 128] NCHW split over the batch; y [16, 256], bias [256]
         B, Cc, H, W = 16, 256, 128, 128
-        y_ = rnd(B, Cc)
+        b0, bn = shard_range(B, d.world, d.rank)
+        y_ = rnd(bn, Cc)
         bias = rnd(Cc)
-        entry("broadcast_binary", f"analog: bf16 x [{B}, {Cc}, {H}, {W}] NCHW, y [{B}, {Cc}], bias [{Cc}]",
-              2 * n * 2 + (B * Cc + Cc) * 2,
-              lambda: (rnd(B, Cc, H, W), torch.empty((B, Cc, H, W), dtype=torch.bfloat16, device=dev)),
-              lambda x, z: hc.broadcast_binary(x, y_, bias, B, z=z))
-    if "activation_gelu_silu" in want:
-        entry("activation_gelu_silu", f"analog: bf16 [{R}, {K}], tanh-GELU", 2 * n * 2,
-              lambda: (rnd(R, K), torch.empty((R, K), dtype=torch.bfloat16, device=dev)),
-              lambda x, y: hc.activation_gelu_silu(x, "gelu", y=y))
-    if "reduce_sum_lastdim" in want:
-        entry("reduce_sum_lastdim", f"analog: bf16 [{R}, {K}] -> fp32 [{R}]", n * 2 + R * 4,
-              lambda: (rnd(R, K), torch.empty((R,), dtype=torch.float32, device=dev)),
-              lambda x, o: hc.reduce_sum_lastdim(x, out=o))
-    if "transpose_2d_4d" in want:
+        ms, (x, z) = timed(lambda: (rnd(bn, Cc, H, W), torch.empty((bn, Cc, H, W), dtype=torch.bfloat16, device=dev)),
+                           lambda x, z: hc.broadcast_binary(x, y_, bias, bn, z=z), 2 * bn * Cc * H * W * 2)
+        ref = (x.float() * y_.float()[:, :, None, None] + bias.float()[None, :, None, None]).to(torch.bfloat16)
+        entry("broadcast_binary", B, bn, Cc * H * W * 2 * 2, ms, exact(ref, z), "hbm")
+    if "activation_gelu_silu" in want:  # tanh-GELU
+        ms, (x, y) = timed(lambda: (rnd(rn, K), torch.empty((rn, K), dtype=torch.bfloat16, device=dev)),
+                           lambda x, y: hc.activation_gelu_silu(x, "gelu", y=y), 2 * rn * K * 2)
+        xd = x[:: max(1, rn // 64)].double()
+        ref = 0.5 * xd * (1.0 + torch.tanh(0.7978845608028654 * (xd + 0.044715 * xd ** 3)))
+        entry("activation_gelu_silu", R, rn, 2 * K * 2, ms, accuracy(ref, y[:: max(1, rn // 64)], 1e-2, 2.0 ** -8), "hbm")
+    if "reduce_sum_lastdim" in want:  # bf16 rows -> fp32 sums
+        ms, (x, o) = timed(lambda: (rnd(rn, K), torch.empty((rn,), dtype=torch.float32, device=dev)),
+                           lambda x, o: hc.reduce_sum_lastdim(x, out=o), rn * K * 2)
+        entry("reduce_sum_lastdim", R, rn, K * 2 + 4, ms, accuracy(x.double().sum(-1), o, 1e-3, 1e-4), "hbm")
+    if "transpose_2d_4d" in want:  # [8192, 8192] bf16 -> [8192, 8192], row blocks split over the ranks
         M = N = 8192
-        entry("transpose_2d_4d", f"analog: bf16 [{M}, {N}] -> [{N}, {M}]", 2 * M * N * 2,
-              lambda: (rnd(M, N), torch.empty((N, M), dtype=torch.bfloat16, device=dev)),
-              lambda x, o: hc.transpose_2d_4d(x, 0, out=o))
-    return out
+        _, mn = shard_range(M, d.world, d.rank)
+        ms, (x, o) = timed(lambda: (rnd(mn, N), torch.empty((N, mn), dtype=torch.bfloat16, device=dev)),
+                           lambda x, o: hc.transpose_2d_4d(x, 0, out=o), 2 * mn * N * 2)
+        entry("transpose_2d_4d", M, mn, N * 2 * 2, ms, exact(x.t().contiguous(), o), "hbm")
 
 
 def run_only(args):
@@ -654,7 +818,7 @@ def run_only(args):
     out = run_extras(hc, d, dev, peaks, args, want=(args.only,))
     hc.check_device_error()
     if d.rank == 0:
-        print(json.dumps({"only": args.only, **out[args.only]}), flush=True)
+        print(json.dumps({"only": args.only, **sig(out[args.only])}), flush=True)
     d.close()
 
 
@@ -667,10 +831,12 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip the non-headline configurations")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-weak", action="store_true", help="with N > 1: skip the weak-scaling (full problem per GPU) figure")
     ap.add_argument("--gather-outputs", action="store_true",
                     help="with N > 1: all-gather every rank's attention output after the timed region and report it")
     ap.add_argument("--fa-batch", type=int, default=FA_B,
-                    help="attention batch per GPU (default 16, the benchmarked size; smaller only for profiling captures)")
+                    help="attention batch of the whole problem (default 16, the benchmarked size; smaller only for "
+                         "profiling captures)")
     ap.add_argument("--only", choices=EXTRA_OPS, default=None,
                     help="time one non-headline configuration alone and print its entry (profiling)")
     args = ap.parse_args()

@@ -218,7 +218,10 @@ int hc_flash_attention_fwd_fused_gqa_launch(const void* q, const void* k, const 
  * and copies o/lse out, pipelined over chunks of (b,h) heads so that transfers overlap the
  * kernel.  `workspace` is a device buffer of at least
  * hc_flash_attention_fwd_fused_host_workspace_size() bytes owned by the caller.  Returns after
- * the outputs are in host memory.  Mirrors the reference runner's host-pointer contract
+ * the outputs are in host memory; after an error it returns only once the work it had queued
+ * is finished, so the workspace and host buffers may be reused at once.  Calls on one device
+ * are serialised inside the library (its internal streams and events are per device).  Mirrors
+ * the reference runner's host-pointer contract
  * (ops/flash_attention_fwd_fused/runner/flash_attention_fwd_fused_runner.hpp:9-18). */
 int hc_flash_attention_fwd_fused_host_workspace_size(
     const struct flash_attention_fwd_fused_tiling_data* t, int dtype, size_t* bytes);
@@ -236,12 +239,16 @@ int hc_flash_attention_fwd_fused_host(const void* h_q, const void* h_k, const vo
  * fail or would synchronise the device.  Copies and kernels run in order on `stream`, one chunk
  * of whole heads at a time (no copy/compute overlap); returns when h_o / h_lse hold the result.
  *   Limit: hc_flash_attention_fwd_fused_host_noalloc_limit() bytes (64 MiB) of staging per
- *   device; a head whose q, k, v, o and lse do not fit is rejected with HC_ERR_UNSUPPORTED
- *   before any device work.
+ *   device; a head whose q, k, v, o and lse do not fit, and every tiling the kernel would
+ *   reject, is refused before any device work.
+ *   The scratch array is part of the library's device image: each device the library is loaded
+ *   on holds those 64 MiB until the process exits, whether or not this entry point is called.
  *   The first call on a device does one-time setup (the scratch's address is looked up with
  *   cudaGetSymbolAddress, the kernel sets its attributes): make it before any stream capture.
- *   Nothing in the scratch needs to start at zero.  Calls that overlap in time on one device
- *   (other threads or streams) race on the single scratch array and must be serialised. */
+ *   The call waits for `stream` to drain before it returns, also after an error once a copy
+ *   was queued.  Nothing in the scratch needs to start at zero.  Calls that overlap in time on
+ *   one device (other threads or streams) race on the single scratch array and must be
+ *   serialised. */
 int hc_flash_attention_fwd_fused_host_noalloc(const void* h_q, const void* h_k, const void* h_v, void* h_o,
                                               float* h_lse,
                                               const struct flash_attention_fwd_fused_tiling_data* t,

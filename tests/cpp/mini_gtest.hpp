@@ -1,6 +1,8 @@
 // A small GoogleTest-compatible test framework (own code; GoogleTest is not installed here).
 //
 // Supports the subset the harness's C++ tests use: TEST, TEST_F (fixtures with SetUp/TearDown),
+// value-parameterized suites (TestWithParam<T>, GetParam(), TEST_P, INSTANTIATE_TEST_SUITE_P with
+// ::testing::Values, named "<prefix>/<Suite>.<name>/<index>" as GoogleTest names them),
 // EXPECT_/ASSERT_ TRUE, FALSE, EQ, NE, LT, LE, GT, GE, NEAR, FLOAT_EQ, DOUBLE_EQ, THROW,
 // NO_THROW, streaming extra context with <<, GTEST_SKIP(), --gtest_filter (':'-separated
 // patterns with * and ?, negatives after '-') and --gtest_list_tests.  Output follows GoogleTest's
@@ -14,6 +16,7 @@
 #include <exception>
 #include <functional>
 #include <iostream>
+#include <memory>
 #include <sstream>
 #include <string>
 #include <vector>
@@ -148,6 +151,89 @@ inline bool& list_only() {
     return l;
 }
 
+// ---- value-parameterized tests --------------------------------------------------------------
+// TEST_P records a pattern per (suite, name); INSTANTIATE_TEST_SUITE_P records the suite's values.
+// The cross product is expanded into ordinary registry entries when the tests are first run, so
+// the order of the two macros in a file does not matter.
+struct ParamPattern {
+    std::string suite, name;
+    std::function<Test*()> make;
+};
+
+inline std::vector<ParamPattern>& param_patterns() {
+    static std::vector<ParamPattern> p;
+    return p;
+}
+
+inline std::vector<std::function<void()>>& param_expansions() {
+    static std::vector<std::function<void()>> e;
+    return e;
+}
+
+inline bool register_param_pattern(const char* suite, const char* name, std::function<Test*()> make) {
+    param_patterns().push_back({suite, name, std::move(make)});
+    return true;
+}
+
+inline void expand_param_tests() {
+    static bool done = false;
+    if (done) return;
+    done = true;
+    for (auto& e : param_expansions()) e();
+}
+
+}  // namespace internal
+
+template <class T>
+class WithParamInterface {
+public:
+    using ParamType = T;
+    virtual ~WithParamInterface() = default;
+    const T& GetParam() const { return *current(); }
+    // The value of the test instance being constructed and run (tests run one at a time).
+    static const T*& current() {
+        static const T* p = nullptr;
+        return p;
+    }
+};
+
+template <class T>
+class TestWithParam : public Test, public WithParamInterface<T> {};
+
+template <class T>
+struct ValueList {
+    std::vector<T> values;
+};
+
+template <class T, class... Ts>
+ValueList<T> Values(T first, Ts... rest) {
+    return ValueList<T>{std::vector<T>{std::move(first), static_cast<T>(std::move(rest))...}};
+}
+
+namespace internal {
+
+template <class Fixture, class T>
+bool register_instantiation(const char* prefix, const char* suite, ValueList<T> list) {
+    using P = typename Fixture::ParamType;
+    auto values = std::make_shared<std::vector<P>>();
+    for (auto& v : list.values) values->push_back(static_cast<P>(v));
+    const std::string pre = prefix, su = suite;
+    param_expansions().push_back([values, pre, su] {
+        for (const auto& pat : param_patterns()) {
+            if (pat.suite != su) continue;
+            for (size_t i = 0; i < values->size(); ++i) {
+                auto make = pat.make;
+                const P* value = &(*values)[i];
+                registry().push_back({pre + "/" + su, pat.name + "/" + std::to_string(i), [make, value, values] {
+                                          WithParamInterface<P>::current() = value;
+                                          return make();
+                                      }});
+            }
+        }
+    });
+    return true;
+}
+
 }  // namespace internal
 
 inline void InitGoogleTest(int* argc, char** argv) {
@@ -160,6 +246,7 @@ inline void InitGoogleTest(int* argc, char** argv) {
 
 inline int RunAllTests() {
     using namespace internal;
+    expand_param_tests();
     std::string pos = filter(), neg;
     const size_t dash = pos.find('-');
     if (dash != std::string::npos) {
@@ -234,6 +321,19 @@ inline int RunAllTests() {
     void MGT_CLASS_(suite, name)::TestBody()
 
 #define TEST(suite, name) MGT_TEST_(suite, name, ::testing::Test)
+
+#define TEST_P(fixture, name)                                                                          \
+    class MGT_CLASS_(fixture, name) : public fixture {                                                 \
+    public:                                                                                            \
+        void TestBody() override;                                                                      \
+    };                                                                                                 \
+    static const bool fixture##_##name##_pattern_ = ::testing::internal::register_param_pattern(      \
+        #fixture, #name, [] { return static_cast<::testing::Test*>(new MGT_CLASS_(fixture, name)); }); \
+    void MGT_CLASS_(fixture, name)::TestBody()
+
+#define INSTANTIATE_TEST_SUITE_P(prefix, fixture, generator)                                       \
+    static const bool prefix##_##fixture##_instantiated_ =                                         \
+        ::testing::internal::register_instantiation<fixture>(#prefix, #fixture, generator)
 #define TEST_F(fixture, name) MGT_TEST_(fixture, name, fixture)
 
 // on_failure is empty for EXPECT_* (continue) and `return` for ASSERT_* (leave the test body).

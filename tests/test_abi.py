@@ -121,3 +121,13 @@ def test_noalloc_runner_limits_are_checked_on_the_host(hc_lib):
         == hc_lib.HC_ERR_INVALID
     assert lib.hc_flash_attention_fwd_fused_host_noalloc(fake, fake, fake, fake, None, C.byref(big), 3, None) \
         == hc_lib.HC_ERR_UNSUPPORTED
+    # tilings the kernel would reject are refused before the first copy is queued (no device here)
+    for bad, status in (((1, 1, 64, 64, 300, 300, 0.05, 0), hc_lib.HC_ERR_UNSUPPORTED),   # D > 256
+                        ((1, 1, 64, 64, 128, 128, 0.05, 2), hc_lib.HC_ERR_INVALID),       # maskType
+                        ((1, 1, 64, 0, 128, 128, 0.05, 1), hc_lib.HC_ERR_INVALID),        # S_k = 0
+                        ((1, 1, 64, 64, 128, 128, float("inf"), 1), hc_lib.HC_ERR_INVALID)):  # scale
+        t = hc_lib.FlashAttentionFwdFusedTiling(*bad)
+        for fn in ("hc_flash_attention_fwd_fused_host_noalloc",):
+            assert getattr(lib, fn)(fake, fake, fake, fake, None, C.byref(t), 2, None) == status, (bad, fn)
+        assert lib.hc_flash_attention_fwd_fused_host(fake, fake, fake, fake, None, C.byref(t), 2, fake, 1 << 30,
+                                                     None) == status, bad

@@ -40,6 +40,21 @@ def _rank_main(rank: int, world: int, port: int, mode: str, q) -> None:
             d.close()
             q.put((rank, "ok" if ok else "bad gather", 0.0, 0.0))
             return
+        if mode == "shard":
+            # strong scaling: the 512 heads of the fixed attention problem and the 8192 GEMM rows
+            # split over the ranks; every unit is owned by exactly one rank
+            import torch
+
+            owned = torch.zeros(512 + 8192 + 4097, dtype=torch.int64)
+            for off, total in ((0, 512), (512, 8192), (512 + 8192, 4097)):
+                s0, cnt = bench.shard_range(total, d.world, rank)
+                owned[off + s0: off + s0 + cnt] += 1
+            d.dist.all_reduce(owned)
+            ms = d.max(10.0 + 5.0 * rank)
+            rate = bench.fixed_job_rate(8.8e12, ms)
+            d.close()
+            q.put((rank, "ok" if bool((owned == 1).all()) else "bad shard", ms, rate))
+            return
         d.barrier()
         ms_local = 10.0 + 5.0 * rank  # rank 1 is the slow one
         ms = d.max(ms_local)
@@ -93,3 +108,30 @@ def test_output_all_gather_two_ranks():
     out, alive = _run(2, "gather", 120)
     assert not alive
     assert sorted(r[:2] for r in out) == [(0, "ok"), (1, "ok")]
+
+
+def test_strong_split_covers_every_unit_once():
+    """The fixed problems split over two gloo ranks (bench.py strong scaling): every attention head,
+    GEMM row and ragged flat range is owned by exactly one rank, and the job's rate is the whole
+    problem's work over the slowest rank's time."""
+    out, alive = _run(2, "shard", 120)
+    assert not alive
+    res = {r[0]: r for r in out}
+    assert set(res) == {0, 1}, out
+    for r in (0, 1):
+        assert res[r][1] == "ok", res[r]
+        assert res[r][3] == pytest.approx(8.8e12 / 15.0e-3)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_shard_range_partitions(world):
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    for total in (0, 1, 7, 512, 8192, 4096 * 8192):
+        spans = [bench.shard_range(total, world, r) for r in range(world)]
+        assert spans[0][0] == 0
+        for (s0, c0), (s1, _) in zip(spans, spans[1:]):
+            assert s0 + c0 == s1
+        assert sum(c for _, c in spans) == total
+        assert max(c for _, c in spans) - min(c for _, c in spans) <= 1

@@ -252,15 +252,26 @@ def test_large_logits_lazy_rescale(cuda, hc_lib, oracle):
         assert_close(ref_lse, lse, 1e-2, 1e-4, "large logits lse")
 
 
-@pytest.mark.parametrize("causal", [1, 0], ids=["causal", "none"])
-def test_full_config_against_simt(cuda, hc_lib, oracle, causal):
-    """Benchmarked configuration: Q, K, V bf16 [16, 32, 8192, 128] ~ N(0,1) (device generator seeds 0/1/2).
-    Sampled heads are recomputed by the fp32-math SIMT kernel (an independent code path pinned
-    to the oracle by test_reference_cases_f32); every row is checked for the convex-combination
-    property min_j V <= O <= max_j V and a finite lse."""
+def _fa_reference_fp64(q, k, v, causal, scale):
+    """softmax(q k^T * scale) v and the natural-log lse of one head ([S, D]) in float64 on the device."""
     import torch
 
-    B, H, S, D = (16, 32, 8192, 128) if causal else (4, 32, 8192, 128)
+    s = (q.double() @ k.double().transpose(0, 1)) * scale
+    if causal:
+        s = s.masked_fill(torch.ones_like(s, dtype=torch.bool).triu(1), float("-inf"))
+    return torch.softmax(s, dim=-1) @ v.double(), torch.logsumexp(s, dim=-1)
+
+
+@pytest.mark.parametrize("causal", [1, 0], ids=["causal", "none"])
+def test_full_config_against_simt(cuda, hc_lib, oracle, causal):
+    """Benchmarked configuration: Q, K, V bf16 [16, 32, 8192, 128] ~ N(0,1) (device generator seeds 0/1/2),
+    causal and non-causal.  32 heads spread over all of batch x heads are recomputed in float64 on the
+    device (a plain softmax(QK^T)V); three of them also by the fp32-math SIMT kernel (an independent
+    code path pinned to the oracle by test_reference_cases_f32); every row is checked for the
+    convex-combination property min_j V <= O <= max_j V and a finite lse."""
+    import torch
+
+    B, H, S, D = 16, 32, 8192, 128
     gens = [torch.Generator(device="cuda").manual_seed(s) for s in (0, 1, 2)]
     q, k, v = (torch.randn((B, H, S, D), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16) for g in gens)
     o, lse = hc_lib.flash_attention_fwd(q, k, v, bool(causal))
@@ -272,6 +283,16 @@ def test_full_config_against_simt(cuda, hc_lib, oracle, causal):
     vmax = v.float().amax(dim=2, keepdim=True)
     of = o.float()
     assert bool(((of >= vmin - 1e-2) & (of <= vmax + 1e-2)).all()), "O outside the convex hull of V"
+    del vmin, vmax, of
+    spread = sorted({(i * B * H // 32 + (i * 7) % (B * H // 32)) for i in range(32)} | {0, B * H - 1})
+    scale = C.default_scale(D)
+    for bh in spread:
+        b, h = divmod(bh, H)
+        o_ref, l_ref = _fa_reference_fp64(q[b, h], k[b, h], v[b, h], bool(causal), scale)
+        err = (o[b, h].double() - o_ref).abs().max().item()
+        lerr = (lse[b, h].double() - l_ref).abs().max().item()
+        assert err <= O_TOL_BF16, (b, h, err)
+        assert lerr <= LSE_TOL, (b, h, lerr)
     heads = [(0, 0), (B - 1, H - 1), (B // 2, 7)]
     for (b, h) in heads:
         qs, ks, vs = (t[b:b + 1, h:h + 1].contiguous().float() for t in (q, k, v))
@@ -310,6 +331,39 @@ def test_host_runner_matches_device(cuda, hc_lib, oracle):
                                                        torch.cuda.current_stream().cuda_stream))
     assert torch.equal(ho.view(torch.int16), o_dev.cpu().view(torch.int16))
     assert torch.equal(hl, lse_dev.cpu())
+
+
+def test_host_runner_error_returns_after_queued_chunks(cuda, hc_lib):
+    """An error in the middle of the chunked host runner (an injected copy failure at chunk 2 of 3)
+    is returned only once the chunks already queued are finished: chunk 1's output is complete in
+    host memory the moment the call returns, so the caller may free the workspace at once."""
+    import ctypes
+
+    import torch
+
+    B, H, S, D = 1, 48, 8192, 128  # 6 MiB of q/k/v per head: 16 heads per ~96 MB chunk, three chunks
+    gens = [torch.Generator(device="cuda").manual_seed(s) for s in (8, 9, 10)]
+    q, k, v = (torch.randn((B, H, S, D), generator=g, device="cuda").to(torch.bfloat16) for g in gens)
+    o_dev, _ = hc_lib.flash_attention_fwd(q, k, v, True)
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ho = torch.full((B, H, S, D), float("nan"), dtype=torch.bfloat16).pin_memory()
+    t = hc_lib.FlashAttentionFwdFusedTiling(B, H, S, S, D, D, C.default_scale(D), 1)
+    lib = hc_lib.load()
+    ws = ctypes.c_size_t()
+    hc_lib.check(lib.hc_flash_attention_fwd_fused_host_workspace_size(ctypes.byref(t), hc_lib.DT_BF16, ctypes.byref(ws)))
+    work = torch.empty(ws.value, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    hc_lib.check(lib.hc_set_fault(b"memcpy:2"))
+    try:
+        st = lib.hc_flash_attention_fwd_fused_host(hq.data_ptr(), hk.data_ptr(), hv.data_ptr(), ho.data_ptr(), None,
+                                                   ctypes.byref(t), hc_lib.DT_BF16, work.data_ptr(), ws.value,
+                                                   torch.cuda.current_stream().cuda_stream)
+        done = ho[:, :16].clone()  # read before any synchronisation of ours
+    finally:
+        lib.hc_set_fault(None)
+    assert st == hc_lib.HC_ERR_INJECTED
+    assert torch.equal(done.view(torch.int16), o_dev[:, :16].cpu().view(torch.int16))
+    del work
 
 
 def test_bounded_wait_reports_timeout(cuda, hc_lib):
