@@ -73,6 +73,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Gives up after `budget_ns` of
 // global time, ORs `code` into *err_word and returns false; the caller then unwinds.
 // `abort_flag` (shared memory) is polled so that once any role of the CTA has given up, the
@@ -92,6 +104,34 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
                 return false;
             }
         }
+    }
+}
+
+// mbar_wait_bounded for a barrier that other CTAs of the cluster arrive on (acquire at cluster
+// scope, so their writes before the arrive are visible after the wait).
+__device__ __forceinline__ bool mbar_wait_bounded_cluster(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
+                                                          uint32_t* err_word, uint32_t code,
+                                                          uint64_t budget_ns = 4000000000ull) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    uint64_t t0 = global_timer_ns();
+    for (uint32_t spins = 1;; ++spins) {
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+        if ((spins & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (global_timer_ns() - t0 > budget_ns) {
+                *abort_flag = 1u;
+                atomicOr(err_word, code);
+                return false;
+            }
+        }
+    }
+}
+
+// Spins for `ns` of global time (bounded pause, e.g. to let copies whose completion this CTA
+// cannot observe land before it exits on an error path).
+__device__ __forceinline__ void spin_ns(uint64_t ns) {
+    const uint64_t t0 = global_timer_ns();
+    while (global_timer_ns() - t0 < ns) {
     }
 }
 
@@ -214,6 +254,107 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
         "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
         "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
         "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// ------------------------------------------------------------------------------------------
+// CTA pairs (cluster of 2 CTAs on two SMs, tcgen05 cta_group::2)
+//
+// A pair computes M = 256 output rows per MMA: CTA rank r holds rows [128 r, 128 r + 128) of the
+// A operand and of the accumulator (its own TMEM lanes 0-127), and half of the B operand
+// (N / 2 columns) in shared memory at the same offsets as its peer.  The even CTA (rank 0)
+// issues the MMAs for both.  TMA loads of both CTAs complete on the even CTA's barrier; the MMA
+// completion is signalled to both CTAs' barriers through tcgen05.commit's CTA mask.  No TMA load
+// here multicasts: each CTA loads only its own half.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_addr), "r"(rank));
+    return d;
+}
+
+// Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Every thread of both CTAs: arrive, then wait for all (release / acquire at cluster scope).
+// The non-.aligned form: threads of a warp may reach it at different times (a role's lane 0
+// leaves its loop after the other lanes).
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// TMA tile load into this CTA's shared memory whose completion (bytes) is counted on the
+// mbarrier at shared::cluster address `bar_cluster`, which may belong to the peer CTA.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster, int32_t c0,
+                                                 int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(tmap), "r"(bar_cluster), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster, int32_t c0,
+                                                 int32_t c1, int32_t c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(tmap), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+// TMEM allocation for the pair: the same warp of both CTAs executes it; each CTA receives the
+// (identical) column address in its own *dst_smem.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Arrives once on the mbarrier at `bar`'s shared-memory offset in every CTA of `cta_mask` when
+// all tcgen05.mma previously issued by this thread for the pair have completed.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(cta_mask)
+        : "memory");
+}
+
+// D(tmem, both CTAs) (+)= A(smem desc, both CTAs) * B(smem desc, N/2 columns in each CTA).
+__device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D(tmem) (+)= A(tmem, each CTA its own 128 rows) * B(smem desc, N/2 columns in each CTA).
+__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 

@@ -256,7 +256,8 @@ int hc_flash_attention_fwd_fused_host_noalloc(const void* h_q, const void* h_k, 
 size_t hc_flash_attention_fwd_fused_host_noalloc_limit(void);
 
 /* Kernel selection used by the last successful flash-attention / matmul_bias launch on this
- * thread: 1 = tcgen05/TMEM path, 2 = SIMT path, 0 = none yet. */
+ * thread: 1 = tcgen05/TMEM path, 2 = SIMT path, 3 = tcgen05 CTA-pair path (matmul_bias with
+ * M >= 256: two SMs per 256x256 tile), 0 = none yet. */
 int hc_flash_attention_last_path(void);
 int hc_matmul_bias_last_path(void);
 

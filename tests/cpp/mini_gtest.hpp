@@ -19,6 +19,8 @@
 #include <memory>
 #include <sstream>
 #include <string>
+#include <type_traits>
+#include <utility>
 #include <vector>
 
 namespace testing {
@@ -103,10 +105,31 @@ private:
     int line_;
 };
 
+// Prints a value for a failure message: with its operator<< when it has one, as its underlying
+// integer for an enum without one, else as "<N-byte object>" (GoogleTest prints bytes).
+template <class T, class = void>
+struct Streamable : std::false_type {};
+template <class T>
+struct Streamable<T, decltype(void(std::declval<std::ostream&>() << std::declval<const T&>()))> : std::true_type {};
+
+template <class T>
+void print_value(std::ostream& os, const T& v) {
+    if constexpr (Streamable<T>::value) {
+        os << v;
+    } else if constexpr (std::is_enum<T>::value) {
+        os << static_cast<long long>(v);
+    } else {
+        os << "<" << sizeof(T) << "-byte object>";
+    }
+}
+
 template <class A, class B>
 std::string cmp_summary(const char* op, const char* ea, const char* eb, const A& a, const B& b) {
     std::ostringstream ss;
-    ss << "Expected: (" << ea << ") " << op << " (" << eb << "), actual: " << a << " vs " << b;
+    ss << "Expected: (" << ea << ") " << op << " (" << eb << "), actual: ";
+    print_value(ss, a);
+    ss << " vs ";
+    print_value(ss, b);
     return ss.str();
 }
 

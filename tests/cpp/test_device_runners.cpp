@@ -356,7 +356,7 @@ TEST(MatmulBiasTest, Bf16TensorCoreOnDevice) {
     DeviceMemory dA = upload(Aq), dB = upload(Bq), db = upload(bq), dC(M * N * 2);
     harness::matmul_bias::run_matmul_bias_device(dA.data(), dB.data(), db.data(), dC.data(), M, K, N, Dtype::BF16);
     ASSERT_TRUE(harness::device::DeviceSynchronize());
-    EXPECT_EQ(hc_matmul_bias_last_path(), 1) << "bf16 with K, N multiples of 8 takes the tcgen05 kernel";
+    EXPECT_EQ(hc_matmul_bias_last_path(), 3) << "bf16 with K, N multiples of 8 and M >= 256 takes the tcgen05 CTA-pair kernel";
     auto got = from_bf16(download<uint16_t>(dC, M * N));
     auto Af = from_bf16(Aq), Bf = from_bf16(Bq), bf = from_bf16(bq);
     std::vector<float> ref(M * N);

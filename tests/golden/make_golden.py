@@ -5,13 +5,15 @@ oracle/_ref/libref_golden.so (this script runs `make` first).  For every test ca
 GTest suites use (tests/cases.py) it records the SHA-256 of the golden's fp32 output bytes plus a
 few leading values, and the generator's own output (so the oracle's data generator is pinned too).
 tests/test_oracle_pins.py recomputes each case with our oracle restatement and requires identical
-bytes.  Run from the repository root:  python tests/golden/make_golden.py [--ref /path/to/reference]
+bytes.  Run from the repository root:  python tests/golden/make_golden.py --ref <reference tree>
+(or with HC_REFERENCE_DIR set)
 """
 from __future__ import annotations
 
 import argparse
 import hashlib
 import json
+import os
 import sys
 from pathlib import Path
 
@@ -138,7 +140,8 @@ def generate(ref) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference", help="path of the reference harness source tree")
+    ap.add_argument("--ref", default=os.environ.get("HC_REFERENCE_DIR"),
+                    help="path of the reference harness source tree (default: $HC_REFERENCE_DIR)")
     a = ap.parse_args()
     import oracle
 

@@ -73,7 +73,7 @@ def _run_device(device: int, hc_lib, oracle, x, out: dict, errors: list):
 
 
 def _check(res, oracle, x):
-    assert res["fa_path"] == 1 and res["mm_path"] == 1, "tensor-core paths not taken"
+    assert res["fa_path"] == 1 and res["mm_path"] == 3, "tensor-core paths not taken (M=384 takes the CTA-pair GEMM)"
     qq, kq, vq = (quantize(a, "bf16", oracle) for a in x["fa"])
     ref, ref_lse = oracle.flash_attention_fwd(qq, kq, vq, 1.0 / np.sqrt(128.0), 1)
     assert_close(ref, res["fa"], 2e-2, 0.0, "flash attention")
