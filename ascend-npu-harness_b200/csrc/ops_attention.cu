@@ -34,6 +34,7 @@
 
 #include <cmath>
 #include <mutex>
+#include <type_traits>
 
 #include "hc_device.cuh"
 #include "hc_internal.h"
@@ -156,7 +157,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // per tile as the tensor core).  Range reduction x = n + f with n = rint(x) obtained by adding
 // 1.5*2^23 (the rounded integer lands in the low mantissa bits), f in [-1/2, 1/2]; 2^f by a cubic
 // whose coefficients are the minimax-relative-error fit on [-1/2, 1/2] from the Remez exchange
-// algorithm (max relative error 7.5e-5, below bf16's 2^-9; derivation: csrc/exp2_poly_fit.py);
+// algorithm (max relative error 7.5e-5, below bf16's 2^-9; derivation: tests/exp2_poly_fit.py);
 // 2^n applied by adding n to the exponent field.  Inputs are clamped to >= -120 so the exponent
 // never underflows; callers only use it where x <= 8.5.
 constexpr float kExp2C0 = 0.99992805719375610f;
@@ -210,15 +211,15 @@ __device__ __forceinline__ void reg_dealloc() {
 }
 
 // Pairs (c, c+1) of a 128-key row may be computed with the FMA-pipe exponential instead of MUFU
-// ex2, selected by bit (pair % 8) of HC_FA_POLY_MASK.  With MUFU alone the two softmax
-// warpgroups need about as many MUFU cycles per KV tile as the tensor core needs for the four
-// MMAs; on B200 every tried mask was slower than MUFU alone (the extra FMA/ALU instructions cost
-// more issue slots than the MUFU wait they hide), so the default mask is empty.
-#ifndef HC_FA_POLY_MASK
-#define HC_FA_POLY_MASK 0x00
-#endif
-// bit (pair % 8) of HC_FA_POLY_MASK set -> that pair uses the FMA-pipe exponential
-__device__ __forceinline__ constexpr bool poly_pair(int pair) { return (HC_FA_POLY_MASK >> (pair & 7)) & 1; }
+// ex2: bit (pair % 8) of the mask selects them.  At D = 64 each score carries half the MMA work of
+// D = 128 while the softmax stream is the same, so the softmax bounds the kernel and moving 1/4 of
+// the exponentials (pairs 0 and 4 of every 8) off MUFU measured +4-5 % on B200.  At D = 128 the
+// tensor pipe's own efficiency bounds the step and every split measured slower, so none is used.
+template <uint32_t HD>
+__device__ __forceinline__ constexpr uint32_t poly_mask() { return HD == 64 ? 0x11u : 0x00u; }
+// bit (pair % 8) of the mask set -> that pair uses the FMA-pipe exponential
+template <uint32_t HD>
+__device__ __forceinline__ constexpr bool poly_pair(int pair) { return (poly_mask<HD>() >> (pair & 7)) & 1; }
 
 template <bool kBF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
@@ -532,26 +533,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float2 negm2 = make_float2(neg_m, neg_m);
                 float2 lsum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
                 // Exponentials 32 keys at a time; each chunk's 16 packed P columns are written back
-                // over S columns already read into registers.
+                // over S columns already read into registers.  kPoly: the FMA-pipe exponential for
+                // the pairs poly_mask selects (unmasked tiles only: masked keys need an exact 0).
+                // The masked / unmasked choice is made once per tile, outside the unrolled loop,
+                // so that each variant is one straight-line block the scheduler can interleave.
+                auto exp_tile = [&](auto poly_tag) {
+                    constexpr bool kPoly = decltype(poly_tag)::value;
 #pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    uint32_t pk[16];
+                    for (int g = 0; g < 4; ++g) {
+                        uint32_t pk[16];
 #pragma unroll
-                    for (int q = 0; q < 16; ++q) {
-                        const int pr = g * 16 + q;
-                        // x = s * scale * log2(e) - m, two keys per packed FMA
-                        float2 x = __ffma2_rn(make_float2(__uint_as_float(sr[2 * pr]), __uint_as_float(sr[2 * pr + 1])),
-                                              scale2, negm2);
-                        if (!masked && poly_pair(pr)) {
-                            x = exp2_poly2(x);
-                        } else {
-                            x.x = ex2(x.x);
-                            x.y = ex2(x.y);
+                        for (int q = 0; q < 16; ++q) {
+                            const int pr = g * 16 + q;
+                            // x = s * scale * log2(e) - m, two keys per packed FMA
+                            float2 x = __ffma2_rn(
+                                make_float2(__uint_as_float(sr[2 * pr]), __uint_as_float(sr[2 * pr + 1])), scale2, negm2);
+                            if (kPoly && poly_pair<HD>(pr)) {
+                                x = exp2_poly2(x);
+                            } else {
+                                x.x = ex2(x.x);
+                                x.y = ex2(x.y);
+                            }
+                            lsum2[q & 1] = __fadd2_rn(lsum2[q & 1], x);
+                            pk[q] = pack2<kBF16>(x.x, x.y);
                         }
-                        lsum2[q & 1] = __fadd2_rn(lsum2[q & 1], x);
-                        pk[q] = pack2<kBF16>(x.x, x.y);
+                        tmem_st16(tS + g * 16, pk);
                     }
-                    tmem_st16(tS + g * 16, pk);
+                };
+                if constexpr (poly_mask<HD>() != 0) {
+                    if (!masked)
+                        exp_tile(std::true_type{});
+                    else
+                        exp_tile(std::false_type{});
+                } else {
+                    exp_tile(std::false_type{});
                 }
                 l += (lsum2[0].x + lsum2[0].y) + (lsum2[1].x + lsum2[1].y);
                 tmem_wait_st();

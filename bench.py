@@ -46,7 +46,11 @@ ROOT = Path(__file__).resolve().parent
 PKG = ROOT / "ascend-npu-harness_b200"
 sys.path.insert(0, str(PKG))
 
-FA_B, FA_H, FA_S, FA_D = 16, 32, 8192, 128
+import specs  # noqa: E402  (per-operator B200 contracts: benchmark configurations and tolerances)
+
+_FA = specs.bench_config("flash_attention_fwd_fused")
+FA_B, FA_H, FA_S, FA_D = _FA["B"], _FA["H"], _FA["S_q"], _FA["D"]
+FA_TOL = specs.tolerance("flash_attention_fwd_fused", "bfloat16")
 METRIC = "flash-attn fwd TFLOP/s (% BF16 peak); norm/RoPE GB/s (% HBM); 1/2/4/8 GPU"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -381,7 +385,8 @@ def fa_reference(q, k, v, causal: bool, scale: float):
 
 
 def check_fa_heads(q, k, v, o, lse, causal: bool, n_sample: int = 4) -> dict:
-    """Sampled heads of this rank's shard ([1, h, S, D]) against fa_reference: O max-abs 2e-2, lse 2e-3."""
+    """Sampled heads of this rank's shard ([1, h, S, D]) against fa_reference, with the spec's bf16
+    tolerances (O max-abs 2e-2, lse 2e-3)."""
     import torch
 
     h = q.shape[1]
@@ -390,12 +395,12 @@ def check_fa_heads(q, k, v, o, lse, causal: bool, n_sample: int = 4) -> dict:
     worst = {"max_abs": 0.0, "max_rel": 0.0, "pass": True, "lse_max_abs": 0.0}
     for i in heads:
         o_ref, l_ref = fa_reference(q[0, i], k[0, i], v[0, i], causal, scale)
-        acc = accuracy(o_ref, o[0, i], 2e-2, 0.0)
+        acc = accuracy(o_ref, o[0, i], FA_TOL["abs"], FA_TOL["rel"])
         lerr = float((l_ref - lse[0, i].double()).abs().max().item())
         worst["max_abs"] = max(worst["max_abs"], acc["max_abs"])
         worst["max_rel"] = max(worst["max_rel"], acc["max_rel"])
         worst["lse_max_abs"] = max(worst["lse_max_abs"], lerr)
-        worst["pass"] = worst["pass"] and acc["pass"] and lerr <= 2e-3
+        worst["pass"] = worst["pass"] and acc["pass"] and lerr <= FA_TOL["lse_abs"]
     worst["heads_checked"] = len(heads)
     return worst
 
@@ -559,7 +564,7 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: Q,K,V ~ N(0,1), torch CUDA generator seeds 0/1/2 (+3 per rank), bf16",
-            "config": {"workload": f"flash_attention_fwd_fused causal bf16 B{args.fa_batch} H32 S8192 D128, "
+            "config": {"workload": f"flash_attention_fwd_fused causal bf16 B{args.fa_batch} H{FA_H} S{FA_S} D{FA_D}, "
                                    f"O bf16 + lse fp32; {total_heads} heads split over {n} GPU(s)",
                        "global_batch": args.fa_batch, "seq_len": FA_S, "heads": FA_H, "head_dim": FA_D,
                        "causal": True, "parallelism": f"dp{n}: batch x heads sharded, no collective",
@@ -652,7 +657,8 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
         del q, k, v, o, lse
 
     if "matmul_bias" in want:  # 8192^3 bf16, M rows split over the ranks, B replicated
-        M = K = N = 8192
+        cfg = specs.bench_config("matmul_bias")
+        M, K, N = cfg["M"], cfg["K"], cfg["N"]
         _, mn = shard_range(M, n, r)
         A = (torch.randn((mn, K), generator=g, device=dev) / math.sqrt(K)).to(torch.bfloat16)
         B = (torch.randn((K, N), generator=g, device=dev) / math.sqrt(K)).to(torch.bfloat16)
@@ -663,12 +669,14 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
         rows = torch.unique(torch.cat([torch.tensor([0, mn - 1]), torch.randint(0, mn, (62,))])).to(dev)
         ref = A[rows].double() @ B.double() + bias.double()
         acc = accuracy(ref, C[rows], 0.0, 0.0)
-        acc["pass"] = float((ref - C[rows].double()).abs().max() / ref.abs().max()) <= 1e-2  # rel-err <= 1e-2
+        acc["pass"] = float((ref - C[rows].double()).abs().max() / ref.abs().max()) <= \
+            specs.tolerance("matmul_bias", "bfloat16")["normwise_rel"]
         entry("matmul_bias", M, mn, 2.0 * N * K, ms, acc, "tensor")
         del A, B, bias, C, ref
 
     if "layer_norm" in want:  # [16384, 4096] bf16, fp32 gamma/beta, rows split over the ranks
-        R, H = 16384, 4096
+        cfg = specs.bench_config("layer_norm")
+        R, H, eps = cfg["rows"], cfg["lastDim"], cfg["eps"]
         _, rn = shard_range(R, n, r)
         gamma = torch.rand((H,), generator=g, device=dev) + 0.5
         beta = torch.rand((H,), generator=g, device=dev) * 0.2 - 0.1
@@ -680,7 +688,7 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
 
         def ln_step():
             xx, yy = nxt()
-            hc.layer_norm(xx, gamma, beta, 1e-5, y=yy)
+            hc.layer_norm(xx, gamma, beta, eps, y=yy)
 
         settle()
         ms = time_launches(ln_step, steps, warm, d, local=True)
@@ -689,17 +697,19 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
         xd = x[rows].double()
         mean = xd.mean(-1, keepdim=True)
         var = ((xd - mean) ** 2).mean(-1, keepdim=True)
-        ref = (xd - mean) / torch.sqrt(var + 1e-5) * gamma.double() + beta.double()
-        acc = accuracy(ref, y[rows], 1e-2, 2.0 ** -8)
+        ref = (xd - mean) / torch.sqrt(var + eps) * gamma.double() + beta.double()
+        tol = specs.tolerance("layer_norm", "bfloat16")
+        acc = accuracy(ref, y[rows], tol["abs"], tol["rel"])
         entry("layer_norm", R, rn, 2 * H * 2 + 2 * H * 4 / rn, ms, acc, "hbm")
         del x, y, sets
 
     if "rms_norm_rope_fused" in want:  # [8, 4096, 32, 128] bf16, rotate-half, positions split over the ranks
-        Bb, S, Hh, D = 8, 4096, 32, 128
+        cfg = specs.bench_config("rms_norm_rope_fused")
+        Bb, S, Hh, D, eps, theta = cfg["B"], cfg["S"], cfg["heads"], cfg["H"], cfg["eps"], cfg["theta"]
         s0, sn = shard_range(S, n, r)
         w = torch.rand((D,), generator=g, device=dev) + 0.5
         pos = torch.arange(S, device=dev, dtype=torch.float32)[:, None]
-        inv = 1.0 / (10000.0 ** (torch.arange(D // 2, device=dev, dtype=torch.float32) * 2 / D))
+        inv = 1.0 / (theta ** (torch.arange(D // 2, device=dev, dtype=torch.float32) * 2 / D))
         cos_all, sin_all = torch.cos(pos * inv), torch.sin(pos * inv)
         cos, sin = cos_all[s0:s0 + sn].contiguous(), sin_all[s0:s0 + sn].contiguous()
         def rms_set():
@@ -710,7 +720,7 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
 
         def rms_step():
             xx, yy = nxt()
-            hc.rms_norm_rope_fused(xx, w, cos, sin, D, 1e-6, heads=Hh, rope_style=1, out=yy)
+            hc.rms_norm_rope_fused(xx, w, cos, sin, D, eps, heads=Hh, rope_style=cfg["rope_style"], out=yy)
 
         settle()
         ms = time_launches(rms_step, steps, warm, d, local=True)
@@ -718,16 +728,17 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
         xs = x[:, :: max(1, sn // 16)].double()  # 16 positions of every batch, all heads
         ys = y[:, :: max(1, sn // 16)]
         cs, ss = cos[:: max(1, sn // 16)].double()[None, :, None], sin[:: max(1, sn // 16)].double()[None, :, None]
-        xn = xs / torch.sqrt((xs * xs).mean(-1, keepdim=True) + 1e-6) * w.double()
+        xn = xs / torch.sqrt((xs * xs).mean(-1, keepdim=True) + eps) * w.double()
         lo, hi = xn[..., : D // 2], xn[..., D // 2:]
         ref = torch.cat([lo * cs - hi * ss, hi * cs + lo * ss], dim=-1)
-        acc = accuracy(ref, ys, 2e-2, 2.0 ** -8)
+        tol = specs.tolerance("rms_norm_rope_fused", "bfloat16")
+        acc = accuracy(ref, ys, tol["abs"], tol["rel"])
         # per (position, head) row: x in and out, plus its share of the position's cos/sin row
         entry("rms_norm_rope_fused", Bb * S * Hh, Bb * sn * Hh, 2 * D * 2 + 2 * (D // 2) * 4 / (Bb * Hh), ms, acc, "hbm")
         del x, y, sets
 
     if "elementwise_add" in want:  # fp16 [4096, 8192], U[-1, 1], flat range split over the ranks
-        total = 4096 * 8192
+        total = math.prod(specs.bench_config("elementwise_add")["shape"])
         _, en = shard_range(total, n, r)
         def add_set():
             a = (torch.rand((en,), generator=g, device=dev) * 2 - 1).to(torch.float16)
@@ -755,7 +766,8 @@ def run_analogs(hc, d: Dist, dev, want, steps, warm, alternate, rotation, entry,
     import torch
 
     g = torch.Generator(device=dev).manual_seed(7 + d.rank)
-    R, K = 16384, 4096  # the layer_norm shape
+    cfg = specs.bench_config("axpy_scalar_affine")
+    R, K = cfg["rows"], cfg["lastDim"]  # the layer_norm shape
     _, rn = shard_range(R, d.world, d.rank)
 
     def rnd(*shape):
@@ -775,10 +787,12 @@ def run_analogs(hc, d: Dist, dev, want, steps, warm, alternate, rotation, entry,
 
     if "axpy_scalar_affine" in want:  # y = 0.5 x - 1 in fp32, one rounding to bf16 (bit-exact)
         ms, (x, y) = timed(lambda: (rnd(rn, K), torch.empty((rn, K), dtype=torch.bfloat16, device=dev)),
-                           lambda x, y: hc.axpy_scalar_affine(x, 0.5, -1.0, y=y), 2 * rn * K * 2)
-        entry("axpy_scalar_affine", R, rn, 2 * K * 2, ms, exact((x.float() * 0.5 + -1.0).to(torch.bfloat16), y), "hbm")
+                           lambda x, y: hc.axpy_scalar_affine(x, cfg["alpha"], cfg["beta"], y=y), 2 * rn * K * 2)
+        ref = (x.float() * cfg["alpha"] + cfg["beta"]).to(torch.bfloat16)
+        entry("axpy_scalar_affine", R, rn, 2 * K * 2, ms, exact(ref, y), "hbm")
     if "broadcast_binary" in want:  # x [16, 256, 128, 128] NCHW split over the batch; y [16, 256], bias [256]
-        B, Cc, H, W = 16, 256, 128, 128
+        bc = specs.bench_config("broadcast_binary")
+        B, Cc, H, W = bc["B"], bc["C"], bc["H"], bc["W"]
         b0, bn = shard_range(B, d.world, d.rank)
         y_ = rnd(bn, Cc)
         bias = rnd(Cc)
@@ -791,13 +805,17 @@ def run_analogs(hc, d: Dist, dev, want, steps, warm, alternate, rotation, entry,
                            lambda x, y: hc.activation_gelu_silu(x, "gelu", y=y), 2 * rn * K * 2)
         xd = x[:: max(1, rn // 64)].double()
         ref = 0.5 * xd * (1.0 + torch.tanh(0.7978845608028654 * (xd + 0.044715 * xd ** 3)))
-        entry("activation_gelu_silu", R, rn, 2 * K * 2, ms, accuracy(ref, y[:: max(1, rn // 64)], 1e-2, 2.0 ** -8), "hbm")
+        tol = specs.tolerance("activation_gelu_silu", "bfloat16")
+        entry("activation_gelu_silu", R, rn, 2 * K * 2, ms, accuracy(ref, y[:: max(1, rn // 64)], tol["abs"], tol["rel"]),
+              "hbm")
     if "reduce_sum_lastdim" in want:  # bf16 rows -> fp32 sums
         ms, (x, o) = timed(lambda: (rnd(rn, K), torch.empty((rn,), dtype=torch.float32, device=dev)),
                            lambda x, o: hc.reduce_sum_lastdim(x, out=o), rn * K * 2)
-        entry("reduce_sum_lastdim", R, rn, K * 2 + 4, ms, accuracy(x.double().sum(-1), o, 1e-3, 1e-4), "hbm")
+        tol = specs.tolerance("reduce_sum_lastdim", "bfloat16")
+        entry("reduce_sum_lastdim", R, rn, K * 2 + 4, ms, accuracy(x.double().sum(-1), o, tol["abs"], tol["rel"]), "hbm")
     if "transpose_2d_4d" in want:  # [8192, 8192] bf16 -> [8192, 8192], row blocks split over the ranks
-        M = N = 8192
+        tc = specs.bench_config("transpose_2d_4d")
+        M, N = tc["M"], tc["N"]
         _, mn = shard_range(M, d.world, d.rank)
         ms, (x, o) = timed(lambda: (rnd(mn, N), torch.empty((N, mn), dtype=torch.bfloat16, device=dev)),
                            lambda x, o: hc.transpose_2d_4d(x, 0, out=o), 2 * mn * N * 2)

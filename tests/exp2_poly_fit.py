@@ -1,8 +1,9 @@
 """Derives the cubic used by exp2_poly2() in ops_attention.cu: the minimax-relative-error
 polynomial p(f) ~ 2^f on [-1/2, 1/2], computed with the Remez exchange algorithm.
 
-The flash-attention softmax evaluates 2^x either on the MUFU unit (ex2.approx) or, for 3/8 of the
-keys, on the FMA pipe as 2^x = 2^n * p(f) with n = rint(x), f = x - n.  Running this script prints
+The flash-attention softmax evaluates 2^x either on the MUFU unit (ex2.approx) or, for 1/4 of the
+keys of unmasked tiles at head dim 64, on the FMA pipe as 2^x = 2^n * p(f) with n = rint(x),
+f = x - n.  Running this script prints
 the four fp32 coefficients and the achieved maximum relative error (about 7.5e-5, well below the
 2^-9 relative precision of the bf16 probabilities the kernel feeds to the tensor core).
 """

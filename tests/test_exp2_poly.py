@@ -1,5 +1,5 @@
 """The FMA-pipe exponential of the flash-attention softmax (exp2_poly2 in ops_attention.cu):
-its constants are the Remez minimax fit that csrc/exp2_poly_fit.py derives, and the exact fp32
+its constants are the Remez minimax fit that tests/exp2_poly_fit.py derives, and the exact fp32
 device sequence (emulated here) stays within 1e-4 relative error of 2^x on the range the kernel
 uses it for.  CPU only."""
 from __future__ import annotations
@@ -11,7 +11,7 @@ from pathlib import Path
 import numpy as np
 
 ROOT = Path(__file__).resolve().parents[1]
-sys.path.insert(0, str(ROOT / "ascend-npu-harness_b200" / "csrc"))
+sys.path.insert(0, str(Path(__file__).resolve().parent))
 
 import exp2_poly_fit as fit  # noqa: E402
 

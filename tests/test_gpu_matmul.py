@@ -51,7 +51,10 @@ def test_matmul_no_bias_and_identity(cuda, hc_lib, oracle):
 def test_matmul_config_sampled_rows(cuda, hc_lib, oracle):
     """Benchmarked configuration: A, B bf16 [8192, 8192] ~ N(0,1)/sqrt(K), bias ~ N(0, 0.1); rel-err <= 1e-2 vs the
     fp32 golden on 128 sampled rows (including rows 0, 1023/1024, 2047/2048, 4095/4096, 8191)."""
-    M = K = N = 8192
+    import specs
+
+    cfg = specs.bench_config("matmul_bias")
+    M, K, N = cfg["M"], cfg["K"], cfg["N"]
     sk = np.float32(1.0 / np.sqrt(K))
     A = (oracle.normal(M * K, 0) * sk).reshape(M, K)
     B = (oracle.normal(K * N, 1) * sk).reshape(K, N)

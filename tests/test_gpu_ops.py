@@ -14,6 +14,7 @@ import numpy as np
 import pytest
 
 import cases as C
+import specs
 from accuracy import assert_close
 from gpu_util import bits, dev, host, quantize
 
@@ -42,9 +43,10 @@ def test_elementwise_add(cuda, hc_lib, oracle, shape, kind):
 
 def test_elementwise_add_config_bit_exact(cuda, hc_lib, oracle):
     """Benchmarked configuration: fp16 [4096, 8192], x ~ U[-1,1] seed 0, y seed 1, bit-exact."""
-    n = 4096 * 8192
-    x = oracle.uniform(n, 0).reshape(4096, 8192)
-    y = oracle.uniform(n, 1).reshape(4096, 8192)
+    shape = tuple(specs.bench_config("elementwise_add")["shape"])  # (4096, 8192)
+    n = int(np.prod(shape))
+    x = oracle.uniform(n, 0).reshape(shape)
+    y = oracle.uniform(n, 1).reshape(shape)
     z = hc_lib.elementwise_add(dev(x, "f16", oracle), dev(y, "f16", oracle))
     ref = oracle.to_f16(oracle.elementwise_add(quantize(x, "f16", oracle), quantize(y, "f16", oracle)))
     assert np.array_equal(bits(z), ref)
@@ -190,7 +192,8 @@ def test_layer_norm_constant_row(cuda, hc_lib, oracle):
 def test_layer_norm_config(cuda, hc_lib, oracle, kind):
     """Benchmarked configuration: bf16 [16384, 4096], x ~ N(0,1) seed 0, gamma ~ U[0.5,1.5], beta ~ U[-0.1,0.1],
     eps 1e-5, max-abs 1e-2 (checked on every row)."""
-    rows, dim = 16384, 4096
+    cfg = specs.bench_config("layer_norm")
+    rows, dim = cfg["rows"], cfg["lastDim"]
     x = oracle.normal(rows * dim, 0).reshape(rows, dim)
     g = oracle.uniform(dim, 1, 0.5, 1.5)
     b = oracle.uniform(dim, 2, -0.1, 0.1)
@@ -230,7 +233,8 @@ def test_rms_norm_rope_heads_and_styles(cuda, hc_lib, oracle, style, H, rot):
 def test_rms_norm_rope_config(cuda, hc_lib, oracle):
     """Benchmarked configuration: x bf16 [8, 4096, 32, 128] ~ N(0,1) seed 0, weight ~ U[0.5,1.5], eps 1e-6,
     rotate-half RoPE theta 10000, fp32 cos/sin; max-abs 2e-2 on every element."""
-    B, S, Hh, D = 8, 4096, 32, 128
+    cfg = specs.bench_config("rms_norm_rope_fused")
+    B, S, Hh, D = cfg["B"], cfg["S"], cfg["heads"], cfg["H"]
     x = oracle.normal(B * S * Hh * D, 0).reshape(B, S, Hh, D)
     w = oracle.uniform(D, 1, 0.5, 1.5)
     cos, sin = oracle.rope_cos_sin(S, D // 2, 10000.0)
