@@ -316,6 +316,10 @@ __global__ void __launch_bounds__(kTmaThreads) transpose16_tma_kernel(const __gr
     // warp w: tile rows 64 (w >> 1) .. +63, column chunks 4 (w & 1) .. +3; lane (rb, jj): 8 x 4
     const uint32_t rb = lane >> 2, j = 4 * (warp & 1) + (lane & 3);
     const uint32_t row0 = 64 * (warp >> 1) + rb * 8;  // first of this lane's eight tile rows (a multiple of 8)
+    // Lanes of odd rb read their eight rows in the order 4..7, 0..3: a 16-byte shared-memory load is
+    // served eight lanes at a time, and with the 128-byte swizzle the two rb of those eight lanes
+    // then address disjoint bank quarters instead of the same ones (+2 % on B200).
+    const uint32_t stag = 4 * (rb & 1);
     uint32_t k = 0;
     for (uint64_t t = blockIdx.x; t < map.total; t += grid, ++k) {
         const uint32_t s = k % kTmaStages;
@@ -329,8 +333,10 @@ __global__ void __launch_bounds__(kTmaThreads) transpose16_tma_kernel(const __gr
             uint32_t a[8][4];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                // row0 + i has (row & 7) == i: its chunk j sits in slot j ^ i
-                const uint4 v = *reinterpret_cast<const uint4*>(st + (row0 + i) * 128 + ((j ^ i) << 4));
+                // a[i] holds tile row row0 + (i ^ stag), whose (row & 7) is i ^ stag: its chunk j sits
+                // in slot j ^ (i ^ stag)
+                const uint32_t ii = i ^ stag;
+                const uint4 v = *reinterpret_cast<const uint4*>(st + (row0 + ii) * 128 + ((j ^ ii) << 4));
                 a[i][0] = v.x;
                 a[i][1] = v.y;
                 a[i][2] = v.z;
@@ -350,6 +356,7 @@ __global__ void __launch_bounds__(kTmaThreads) transpose16_tma_kernel(const __gr
                     o.y = __byte_perm(a[2][w], a[3][w], sel);
                     o.z = __byte_perm(a[4][w], a[5][w], sel);
                     o.w = __byte_perm(a[6][w], a[7][w], sel);
+                    if (stag) o = make_uint4(o.z, o.w, o.x, o.y);  // rows 4..7 came first
                     __stcs(reinterpret_cast<uint4*>(dst + static_cast<size_t>(c) * R), o);
                 }
             }
