@@ -29,7 +29,9 @@ def _rel_err(ref, got):
 
 @pytest.mark.parametrize("kind", ["bf16", "f16"])
 @pytest.mark.parametrize("M,K,N", [(16, 16, 16), (64, 64, 64), (128, 128, 128), (256, 64, 16), (1, 1024, 64),
-                                   (64, 32, 128), (256, 256, 64), (300, 200, 264), (129, 72, 520), (1000, 1024, 1000)])
+                                   (64, 32, 128), (256, 256, 64), (300, 200, 264), (129, 72, 520), (1000, 1024, 1000),
+                                   # CTA-pair kernel edges: one pair tile, K of one partial block, M/N/K tails
+                                   (256, 8, 256), (257, 72, 1000), (512, 8, 264), (2048, 4104, 520), (768, 64, 8)])
 def test_matmul_tensor_core(cuda, hc_lib, oracle, M, K, N, kind):
     A, B, bias = C.matmul_inputs(oracle, M, K, N)
     out = hc_lib.matmul_bias(dev(A, kind, oracle), dev(B, kind, oracle), dev(bias, kind, oracle))
