@@ -36,6 +36,9 @@ int get_pipe(Pipe** out, std::unique_lock<std::mutex>* lock) {
     if (dev < 0 || dev >= 64) return fail(HC_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
     Pipe& p = g_pipes[dev];
     *lock = std::unique_lock<std::mutex>(p.mu);
+    // A thread that has not used the runtime yet has no context bound (id 0); selecting the
+    // current device binds its primary context, so the comparison below sees the real id.
+    HC_CHECK_CUDA(cudaSetDevice(dev));
     const uint64_t ctx = current_context_id();
     if (p.ctx == 0 || ctx == 0 || p.ctx != ctx) {
         // First use on this device, or the device was reset since (the old handles died with the
@@ -227,6 +230,7 @@ int noalloc_scratch(void** out) {
     if (dev < 0 || dev >= 64) return fail(HC_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     ScratchAddr& a = g_noalloc_addr[dev];
+    HC_CHECK_CUDA(cudaSetDevice(dev));  // binds the device's primary context to a thread new to the runtime
     const uint64_t ctx = current_context_id();
     if (!a.ptr || ctx == 0 || a.ctx != ctx) {
         void* p = nullptr;
