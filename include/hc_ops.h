@@ -255,6 +255,23 @@ int hc_flash_attention_fwd_fused_host_noalloc(const void* h_q, const void* h_k, 
                                               int dtype, void* stream);
 size_t hc_flash_attention_fwd_fused_host_noalloc_limit(void);
 
+/* Backward of hc_flash_attention_fwd_fused_launch (no counterpart in the reference: its ladder is
+ * forward only).  From q, k, v, the forward's o and lse (natural log) and the output gradient
+ * dO [B,H,S_q,D_v], writes dq [B,H,S_q,D], dk [B,H,S_k,D], dv [B,H,S_k,D_v] (all in `dtype`, every
+ * element written) and delta [B,H,S_q] fp32 = rowsum(dO * o), a caller-owned buffer the second
+ * kernel reads:  P = exp(S * scale - lse), dv = P^T dO, dS = P * (dO V^T - delta),
+ * dq = scale * dS K, dk = scale * dS^T Q.  Same tiling record and checks as the forward
+ * (K/V have H heads; grouped-query heads are not supported here).
+ * dtype BF16 or F16 with D = D_v = 128 (16-byte aligned buffers) -> two tcgen05/TMEM kernels
+ * (dq+delta, then dk/dv), P and dS rounded to `dtype` for the tensor-core products as the
+ * forward rounds P; other D/D_v (<= 256) or F32 -> SIMT kernels in fp32. */
+int hc_flash_attention_bwd_launch(const void* q, const void* k, const void* v, const void* o,
+                                  const void* dO, const float* lse, void* dq, void* dk, void* dv,
+                                  float* delta, const struct flash_attention_fwd_fused_tiling_data* t,
+                                  int dtype, void* stream);
+/* Kernel selection of the last successful backward launch on this thread (1 tcgen05, 2 SIMT). */
+int hc_flash_attention_bwd_last_path(void);
+
 /* Kernel selection used by the last successful flash-attention / matmul_bias launch on this
  * thread: 1 = tcgen05/TMEM path, 2 = SIMT path, 3 = tcgen05 CTA-pair path (matmul_bias with
  * M >= 256: two SMs per 256x256 tile), 0 = none yet. */

@@ -329,6 +329,62 @@ static void fa_heads(const float* Q, const float* K, const float* V, float* O, f
     }
 }
 
+// ------------------------------------------------------------------------------------------
+// flash attention backward (no reference golden exists: the harness has no backward).  The
+// exact gradients of O = softmax(Q K^T * scale [+ causal mask]) V in fp64 for given dO:
+//   P = softmax(S) row-wise, dV = P^T dO, dP = dO V^T, Delta = rowsum(P * dP) (= rowsum(dO * O)),
+//   dS = P * (dP - Delta), dQ = scale * dS K, dK = scale * dS^T Q.
+// ------------------------------------------------------------------------------------------
+void oracle_flash_attention_bwd(const float* Q, const float* K, const float* V, const float* dO, float* dQ, float* dK,
+                                float* dV, int64_t B, int64_t H, int64_t S_q, int64_t S_k, int64_t D, int64_t D_v,
+                                float scale, int mask) {
+    std::vector<double> p(static_cast<size_t>(S_k)), dp(static_cast<size_t>(S_k));
+    std::vector<double> gk(static_cast<size_t>(S_k * D)), gv(static_cast<size_t>(S_k * D_v));
+    for (int64_t bh = 0; bh < B * H; ++bh) {
+        const float* Qh = Q + bh * S_q * D;
+        const float* Kh = K + bh * S_k * D;
+        const float* Vh = V + bh * S_k * D_v;
+        const float* dOh = dO + bh * S_q * D_v;
+        std::fill(gk.begin(), gk.end(), 0.0);
+        std::fill(gv.begin(), gv.end(), 0.0);
+        for (int64_t r = 0; r < S_q; ++r) {
+            const int64_t nk = (mask == 1) ? std::min(S_k, r + 1) : S_k;
+            double mx = -1e300;
+            for (int64_t k = 0; k < nk; ++k) {
+                double dot = 0.0;
+                for (int64_t d = 0; d < D; ++d) dot += static_cast<double>(Qh[r * D + d]) * Kh[k * D + d];
+                p[k] = dot * scale;
+                mx = std::max(mx, p[k]);
+            }
+            double l = 0.0;
+            for (int64_t k = 0; k < nk; ++k) {
+                p[k] = std::exp(p[k] - mx);
+                l += p[k];
+            }
+            double delta = 0.0;
+            for (int64_t k = 0; k < nk; ++k) {
+                p[k] /= l;
+                double dot = 0.0;
+                for (int64_t d = 0; d < D_v; ++d) dot += static_cast<double>(dOh[r * D_v + d]) * Vh[k * D_v + d];
+                dp[k] = dot;
+                delta += p[k] * dot;
+            }
+            for (int64_t d = 0; d < D; ++d) {
+                double g = 0.0;
+                for (int64_t k = 0; k < nk; ++k) g += p[k] * (dp[k] - delta) * Kh[k * D + d];
+                dQ[(bh * S_q + r) * D + d] = static_cast<float>(g * scale);
+            }
+            for (int64_t k = 0; k < nk; ++k) {
+                const double ds = p[k] * (dp[k] - delta) * scale;
+                for (int64_t d = 0; d < D; ++d) gk[k * D + d] += ds * Qh[r * D + d];
+                for (int64_t d = 0; d < D_v; ++d) gv[k * D_v + d] += p[k] * dOh[r * D_v + d];
+            }
+        }
+        for (int64_t i = 0; i < S_k * D; ++i) dK[bh * S_k * D + i] = static_cast<float>(gk[i]);
+        for (int64_t i = 0; i < S_k * D_v; ++i) dV[bh * S_k * D_v + i] = static_cast<float>(gv[i]);
+    }
+}
+
 void oracle_flash_attention_fwd(const float* Q, const float* K, const float* V, float* O, float* lse, int64_t B,
                                 int64_t H, int64_t S_q, int64_t S_k, int64_t D, int64_t D_v, float scale, int mask) {
     fa_heads(Q, K, V, O, lse, 0, B * H, S_q, S_k, D, D_v, scale, mask);

@@ -60,6 +60,11 @@ void oracle_rms_norm_rope(const float* x, const float* weight, const float* cos_
 /* ops/matmul_bias/golden/matmul_bias_golden.cpp:6-27 (bias may be NULL) */
 void oracle_matmul_bias(const float* A, const float* B, const float* bias, float* C, int64_t M, int64_t K,
                         int64_t N);
+/* Flash-attention backward in fp64: exact dQ, dK, dV of softmax(Q K^T * scale [causal]) V for dO (the
+ * harness has no backward golden; this restates the gradients from the definition). */
+void oracle_flash_attention_bwd(const float* Q, const float* K, const float* V, const float* dO, float* dQ, float* dK,
+                                float* dV, int64_t B, int64_t H, int64_t S_q, int64_t S_k, int64_t D, int64_t D_v,
+                                float scale, int mask);
 /* ops/flash_attention_fwd_fused/golden/flash_attention_fwd_fused_golden.cpp:10-112, plus
  * lse = m + ln(l) per row (may be NULL).  mask 0 none, 1 causal. */
 void oracle_flash_attention_fwd(const float* Q, const float* K, const float* V, float* O, float* lse, int64_t B,

@@ -64,6 +64,7 @@ class Oracle:
         fa_args = [_f32p, _f32p, _f32p, _f32p, C.c_void_p, _i64, _i64, _i64, _i64, _i64, _i64, C.c_float, C.c_int]
         lib.oracle_flash_attention_fwd.argtypes = fa_args
         lib.oracle_flash_attention_fwd_mt.argtypes = fa_args + [C.c_int]
+        lib.oracle_flash_attention_bwd.argtypes = [_f32p] * 7 + [_i64] * 6 + [C.c_float, C.c_int]
 
     # ---- generators / codecs ----
     def uniform(self, n, seed, lo=-1.0, hi=1.0):
@@ -195,6 +196,17 @@ class Oracle:
         else:
             self.lib.oracle_flash_attention_fwd(*args)
         return o, lse
+
+    def flash_attention_bwd(self, q, k, v, do, scale, causal):
+        """q [B,H,S_q,D], k [B,H,S_k,D], v [B,H,S_k,D_v], dO [B,H,S_q,D_v] -> (dQ, dK, dV), fp64 math."""
+        q, k, v, do = _f32(q), _f32(k), _f32(v), _f32(do)
+        B, H, S_q, D = q.shape
+        S_k, D_v = k.shape[2], v.shape[3]
+        dq, dk, dv = np.empty_like(q), np.empty_like(k), np.empty_like(v)
+        self.lib.oracle_flash_attention_bwd(q.reshape(-1), k.reshape(-1), v.reshape(-1), do.reshape(-1),
+                                            dq.reshape(-1), dk.reshape(-1), dv.reshape(-1), B, H, S_q, S_k, D, D_v,
+                                            scale, 1 if causal else 0)
+        return dq, dk, dv
 
 
 class Reference:

@@ -81,6 +81,27 @@ def test_flash_attention_lse_definition(oracle):
         np.testing.assert_allclose(lse, ref, rtol=1e-6, atol=1e-6)
 
 
+@pytest.mark.parametrize("shape", [(1, 2, 37, 37, 16, 16), (2, 1, 20, 45, 8, 12), (1, 1, 45, 20, 12, 8)])
+@pytest.mark.parametrize("causal", [0, 1])
+def test_flash_attention_bwd_against_autograd(oracle, shape, causal):
+    """The backward oracle (no reference counterpart: the ladder is forward only) against torch
+    float64 autograd of the same forward, top-left causal mask as the reference golden."""
+    import torch
+
+    B, H, S_q, S_k, D, Dv = shape
+    q, k, v = C.fa_inputs(oracle, B, H, S_q, S_k, D, Dv)
+    do = oracle.uniform(B * H * S_q * Dv, 99).reshape(B, H, S_q, Dv)
+    scale = 0.3
+    dq, dk, dv = oracle.flash_attention_bwd(q, k, v, do, scale, causal)
+    tq, tk, tv = (torch.tensor(a, dtype=torch.float64, requires_grad=True) for a in (q, k, v))
+    s = tq @ tk.transpose(-1, -2) * float(np.float32(scale))
+    if causal:
+        s = s.masked_fill(torch.ones(S_q, S_k, dtype=torch.bool).triu(1), float("-inf"))
+    (torch.softmax(s, -1) @ tv).backward(torch.tensor(do, dtype=torch.float64))
+    for got, ref in ((dq, tq.grad), (dk, tk.grad), (dv, tv.grad)):
+        np.testing.assert_allclose(got, ref.numpy(), rtol=1e-5, atol=1e-6)
+
+
 @pytest.mark.parametrize("case", C.MATMUL_CASES, ids=lambda c: "M{}_K{}_N{}_{}".format(c[0], c[1], c[2], "bias" if c[3] else "nobias"))
 def test_matmul_bias_pinned(oracle, case):
     M, K, N, wb = case
