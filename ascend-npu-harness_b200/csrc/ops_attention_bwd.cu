@@ -15,10 +15,16 @@
 //     kernel: for every query block i that sees the keys: S^T = K Q_i^T and dP^T = V dO_i^T,
 //     P^T and dS^T (16-bit) over them, dV += P^T dO_i and dK += dS^T Q_i, accumulated in TMEM
 //     (S^T, dP^T, dV, dK = 512 columns) and written once at the end.
-// Roles per CTA: warps 0-3 the elementwise work (one TMEM lane = one row or key per thread),
-// warp 4 issues tcgen05.mma, warp 5 issues TMA (no multicast).  Work units are handed out as
-// complementary block pairs (b, n-1-b) of one head so that every CTA gets the same causal work.
-// Every mbarrier wait is bounded as in the forward kernel.
+// Roles per CTA: two elementwise warpgroups (warps 0-3 and 4-7; a thread owns one TMEM lane, i.e.
+// one row or key, and warpgroup g the 64 columns [64g, 64g+64) of every 128-column tile), warp 8
+// issues tcgen05.mma, warp 9 issues TMA (no multicast).  Each warpgroup writes its 16-bit half of
+// P / dS into its own columns, and the MMA warp issues the TMEM-operand products half by half (K
+// steps 0-3 after warpgroup 0, 4-7 after warpgroup 1).  The causal mask is applied only on the
+// diagonal block; tails need none (rows past S_q get lse = +inf, so P = 0; keys past S_k only
+// reach accumulator rows that are not stored, or meet zero K/V rows).  Work units are handed out
+// as complementary block pairs (b, n-1-b) of one head so that every CTA gets the same causal work.
+// Every mbarrier wait is bounded as in the forward kernel, and the two warpgroups take every
+// give-up decision together (a barrier that ANDs their results), so none is left at a barrier.
 //
 // SIMT path: fp32, or any other head dims (<= 256): a warp per query row for dQ/Delta and a
 // warp per key row for dK/dV, fp32 math.
@@ -29,6 +35,7 @@
 
 #include <cmath>
 #include <mutex>
+#include <type_traits>
 
 #include "hc_device.cuh"
 #include "hc_internal.h"
@@ -43,13 +50,16 @@ using namespace sm100;
 constexpr uint32_t kBlk = 128;                  // rows (queries or keys) per block
 constexpr uint32_t kPanelBytes = 128 * 64 * 2;  // one 64-column swizzle panel of a 128-row tile: 16 KB
 constexpr uint32_t kTileBytes = 2 * kPanelBytes;  // a 128 x 128 16-bit tile: 32 KB
-constexpr uint32_t kThreads = 192;
+constexpr uint32_t kElemThreads = 256;          // two elementwise warpgroups
+constexpr uint32_t kMmaWarp = 8, kTmaWarp = 9;
+constexpr uint32_t kThreads = 320;
 constexpr uint32_t kStages = 4;                 // streamed-tile ring
 constexpr uint32_t kOffFixed = 0;               // two tiles resident per unit (Q,dO or K,V)
 constexpr uint32_t kOffRing = 2 * kTileBytes;
 constexpr uint32_t kOffBar = kOffRing + kStages * kTileBytes;
-constexpr uint32_t kOffVec = kOffBar + 256;      // per-block lse/Delta staging (dK/dV kernel)
-constexpr uint32_t kSmemBytes = kOffVec + 2 * kBlk * 4 + 1024;
+constexpr uint32_t kOffVec = kOffBar + 256;     // dQ: Delta halves; dK/dV: -lse*log2(e) and Delta, double-buffered
+constexpr uint32_t kVecBytes = 2 * 2 * kBlk * 4;
+constexpr uint32_t kSmemBytes = kOffVec + kVecBytes + 1024;
 
 enum : uint32_t {
     kErrProducer = 1u << 0,
@@ -73,7 +83,7 @@ struct Params {
 struct Bars {
     uint64_t fixed_full, fixed_empty;
     uint64_t ring_full[kStages], ring_empty[kStages];
-    uint64_t sdp_full, ds_full, acc_full;
+    uint64_t sdp_full, ds_half[2], acc_full;
     uint64_t mma_done;
 };
 
@@ -135,14 +145,17 @@ __device__ __forceinline__ void issue_ss(uint32_t d_tmem, uint32_t a_addr, uint3
     }
 }
 
-// D (M=128, N=128) (+)= A (128 x 128 16-bit in TMEM, K along columns) * B (128 K-rows x 128, MN-major smem).
-__device__ __forceinline__ void issue_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, uint32_t idesc,
-                                         bool accumulate) {
+// Half h of D (M=128, N=128) (+)= A * B over K: A is the 16-bit tile in TMEM whose K range
+// [64h, 64h+64) sits in columns [64h, 64h+32) of `a_tmem` (each warpgroup packs its half of P or dS
+// into its own columns); B holds K rows [64h, 64h+64) of a 128-row MN-major smem tile.  K-steps
+// 4h..4h+3; `accumulate` false only for the first half of a fresh accumulator.
+__device__ __forceinline__ void issue_ts_half(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, uint32_t idesc,
+                                              uint32_t h, bool accumulate) {
     const Sw128Desc bd = make_sw128_desc2(b_addr, kPanelBytes, 1024);
 #pragma unroll
-    for (uint32_t kk = 0; kk < 8; ++kk)
-        mma_ts2(d_tmem, a_tmem + kk * 8, Sw128Desc{bd.lo + kk * (2048 >> 4), bd.hi}, idesc,
-                (accumulate || kk > 0) ? 1u : 0u);
+    for (uint32_t s = 0; s < 4; ++s)
+        mma_ts2(d_tmem, a_tmem + h * 64 + s * 8, Sw128Desc{bd.lo + (4 * h + s) * (2048 >> 4), bd.hi}, idesc,
+                (accumulate || s > 0) ? 1u : 0u);
 }
 
 __device__ __forceinline__ uint32_t n_blocks(uint32_t S) { return (S + kBlk - 1) / kBlk; }
@@ -167,23 +180,108 @@ __device__ __forceinline__ uint4 tile_chunk(const uint8_t* tile, uint32_t row, u
     return *reinterpret_cast<const uint4*>(tile + (c >> 3) * kPanelBytes + row * 128 + (((c & 7) ^ (row & 7)) << 4));
 }
 
-// Barrier among the 128 threads of the elementwise warpgroup only.
-__device__ __forceinline__ void wg_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier among the 256 elementwise threads only (named barrier 1).
+__device__ __forceinline__ void ew_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-// The same barrier, returning the AND of `pred` over the warpgroup: every warp takes the same
+// The same barrier, returning the AND of `pred` over both warpgroups: every warp takes the same
 // branch after it, so no warp can leave a loop that still has a barrier another warp waits on.
-__device__ __forceinline__ bool wg_all(bool pred) {
+__device__ __forceinline__ bool ew_all(bool pred) {
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.and.pred q, 1, 128, p;\n\t"
+        "bar.red.and.pred q, 1, 256, p;\n\t"
         "selp.u32 %0, 1, 0, q;\n\t}"
         : "=r"(r)
         : "r"(static_cast<uint32_t>(pred))
         : "memory");
     return r != 0;
 }
+
+// Shared setup of both kernels: barriers, TMEM (512 columns, warp 8), and the bounded-wait state.
+__device__ __forceinline__ uint32_t setup_cta(Bars* bars, uint32_t* tmem_slot, volatile uint32_t* abort_flag,
+                                              uint32_t warp) {
+    if (threadIdx.x == 0) {
+        mbar_init(&bars->fixed_full, 1);
+        mbar_init(&bars->fixed_empty, 1);
+        for (uint32_t s = 0; s < kStages; ++s) {
+            mbar_init(&bars->ring_full[s], 1);
+            mbar_init(&bars->ring_empty[s], 1);
+        }
+        mbar_init(&bars->sdp_full, 1);
+        mbar_init(&bars->ds_half[0], 128);
+        mbar_init(&bars->ds_half[1], 128);
+        mbar_init(&bars->acc_full, 1);
+        mbar_init(&bars->mma_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    return *tmem_slot;
+}
+
+__device__ __forceinline__ void teardown_cta(uint32_t tmem_base, uint32_t warp) {
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarp) {
+        __syncwarp();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+// The producer's wait for a free ring slot, its loads, and the drain after a give-up: every
+// issued load is waited for (bounded) so no copy lands in shared memory after the CTA exits.
+struct Ring {
+    uint32_t stage = 0, phase = 0, pend_valid = 0, pend_phase = 0;
+    __device__ __forceinline__ bool load(Bars* bars, uint8_t* smem, const CUtensorMap* tm, uint32_t row_blk,
+                                         uint32_t bh, volatile uint32_t* abort_flag) {
+        if (!mbar_wait_bounded(&bars->ring_empty[stage], phase ^ 1, abort_flag, &g_fab_error_word, kErrProducer))
+            return false;
+        mbar_arrive_expect_tx(&bars->ring_full[stage], kTileBytes);
+        for (uint32_t h = 0; h < 2; ++h)
+            tma_load_3d(smem + kOffRing + stage * kTileBytes + h * kPanelBytes, tm, &bars->ring_full[stage], h * 64,
+                        row_blk * kBlk, bh);
+        pend_valid |= 1u << stage;
+        pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
+        if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+        }
+        return true;
+    }
+    __device__ __forceinline__ void drain(Bars* bars, int32_t fixed_pending) {
+        volatile uint32_t never = 0;
+        for (uint32_t s = 0; s < kStages; ++s)
+            if (pend_valid & (1u << s))
+                mbar_wait_bounded(&bars->ring_full[s], (pend_phase >> s) & 1u, &never, &g_fab_error_word, kErrDrain,
+                                  1000000000ull);
+        if (fixed_pending >= 0)
+            mbar_wait_bounded(&bars->fixed_full, static_cast<uint32_t>(fixed_pending), &never, &g_fab_error_word,
+                              kErrDrain, 1000000000ull);
+    }
+};
+
+// The MMA warp's consumer side of the ring.
+struct RingWait {
+    uint32_t stage = 0, phase = 0;
+    __device__ __forceinline__ bool next(Bars* bars, volatile uint32_t* abort_flag, uint32_t& st) {
+        if (!mbar_wait_bounded(&bars->ring_full[stage], phase, abort_flag, &g_fab_error_word, kErrMma)) return false;
+        tc_fence_after();
+        st = stage;
+        if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+        }
+        return true;
+    }
+};
 
 // ============================================================================================
 // dQ (and Delta)
@@ -198,34 +296,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + sizeof(Bars));
     volatile uint32_t* abort_flag = tmem_slot + 1;
+    float* s_part = reinterpret_cast<float*>(smem + kOffVec);  // [2][128] Delta halves
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        mbar_init(&bars->fixed_full, 1);
-        mbar_init(&bars->fixed_empty, 1);
-        for (uint32_t s = 0; s < kStages; ++s) {
-            mbar_init(&bars->ring_full[s], 1);
-            mbar_init(&bars->ring_empty[s], 1);
-        }
-        mbar_init(&bars->sdp_full, 1);
-        mbar_init(&bars->ds_full, 128);
-        mbar_init(&bars->acc_full, 1);
-        mbar_init(&bars->mma_done, 1);
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    if (warp == 4) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t tmem_base = setup_cta(bars, tmem_slot, abort_flag, warp);
     const uint32_t sQ = smem_u32(smem + kOffFixed), sDO = sQ + kTileBytes, sRing = smem_u32(smem + kOffRing);
-    // TMEM: S [0,128), dP [128,256), dQ [256,384); dS (16-bit) overlays S.
-    if (warp == 5) {
+    // TMEM: S [0,128), dP [128,256), dQ [256,384); dS (16-bit) of warpgroup g in S columns [64g, 64g+32).
+    if (warp == kTmaWarp) {
         if (lane == 0) {
-            uint32_t stage = 0, phase = 0, it = 0, pend_valid = 0, pend_phase = 0;
+            Ring ring;
+            uint32_t it = 0;
             int32_t fixed_pending = -1;
             bool ok = true;
             Units u(blockIdx.x);
@@ -243,55 +322,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 fixed_pending = static_cast<int32_t>(it & 1);
                 const uint32_t nkv = kv_blocks_for(p, qb);
-                for (uint32_t j = 0; j < nkv && ok; ++j) {
-                    for (uint32_t kv = 0; kv < 2; ++kv) {  // K_j, then V_j
-                        if (!mbar_wait_bounded(&bars->ring_empty[stage], phase ^ 1, abort_flag, &g_fab_error_word,
-                                               kErrProducer)) {
-                            ok = false;
-                            break;
-                        }
-                        mbar_arrive_expect_tx(&bars->ring_full[stage], kTileBytes);
-                        for (uint32_t h = 0; h < 2; ++h)
-                            tma_load_3d(smem + kOffRing + stage * kTileBytes + h * kPanelBytes, kv ? &tm_v : &tm_k,
-                                        &bars->ring_full[stage], h * 64, j * kBlk, bh);
-                        pend_valid |= 1u << stage;
-                        pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
-                        if (++stage == kStages) {
-                            stage = 0;
-                            phase ^= 1;
-                        }
-                    }
-                }
+                for (uint32_t j = 0; j < nkv && ok; ++j)  // K_j, then V_j
+                    ok = ring.load(bars, smem, &tm_k, j, bh, abort_flag) && ring.load(bars, smem, &tm_v, j, bh, abort_flag);
             }
-            if (!ok) {
-                volatile uint32_t never = 0;
-                for (uint32_t s = 0; s < kStages; ++s)
-                    if (pend_valid & (1u << s))
-                        mbar_wait_bounded(&bars->ring_full[s], (pend_phase >> s) & 1u, &never, &g_fab_error_word,
-                                          kErrDrain, 1000000000ull);
-                if (fixed_pending >= 0)
-                    mbar_wait_bounded(&bars->fixed_full, static_cast<uint32_t>(fixed_pending), &never,
-                                      &g_fab_error_word, kErrDrain, 1000000000ull);
-            }
+            if (!ok) ring.drain(bars, fixed_pending);
         }
-    } else if (warp == 4) {
+    } else if (warp == kMmaWarp) {
         if (lane == 0) {
             const uint32_t idesc_ss = make_idesc_f16(kBF16, 128, 128, false, false);
             const uint32_t idesc_ts = make_idesc_f16(kBF16, 128, 128, false, true);
             const uint32_t tS = tmem_base, tDP = tmem_base + 128, tDQ = tmem_base + 256;
-            uint32_t stage = 0, phase = 0, it = 0, ds_par = 0;
+            RingWait ring;
+            uint32_t it = 0, ds_par = 0;
             bool ok = true;
-            auto wait_ring = [&](uint32_t& st) -> bool {
-                if (!mbar_wait_bounded(&bars->ring_full[stage], phase, abort_flag, &g_fab_error_word, kErrMma))
-                    return false;
-                tc_fence_after();
-                st = stage;
-                if (++stage == kStages) {
-                    stage = 0;
-                    phase ^= 1;
-                }
-                return true;
-            };
             Units u(blockIdx.x);
             uint32_t bh, qb;
             for (; ok && u.next(p, bh, qb); ++it) {
@@ -303,21 +346,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t nkv = kv_blocks_for(p, qb);
                 for (uint32_t j = 0; j < nkv; ++j) {
                     uint32_t ks, vs;
-                    if (!wait_ring(ks)) { ok = false; break; }
+                    if (!ring.next(bars, abort_flag, ks)) { ok = false; break; }
                     issue_ss(tS, sQ, sRing + ks * kTileBytes, idesc_ss);              // S = Q K_j^T
-                    if (!wait_ring(vs)) { ok = false; break; }
+                    if (!ring.next(bars, abort_flag, vs)) { ok = false; break; }
                     issue_ss(tDP, sDO, sRing + vs * kTileBytes, idesc_ss);            // dP = dO V_j^T
                     tc_commit(&bars->sdp_full);
-                    if (!mbar_wait_bounded(&bars->ds_full, ds_par, abort_flag, &g_fab_error_word, kErrMma)) {
-                        ok = false;
-                        break;
+                    for (uint32_t h = 0; h < 2 && ok; ++h) {                         // dQ += dS K_j, by key halves
+                        if (!mbar_wait_bounded(&bars->ds_half[h], ds_par, abort_flag, &g_fab_error_word, kErrMma)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        // Q and dO are free once the last dP is done and both warpgroups, which read
+                        // dO for Delta before their first dS, have arrived.
+                        if (h == 1 && j + 1 == nkv) tc_commit(&bars->fixed_empty);
+                        issue_ts_half(tDQ, tS, sRing + ks * kTileBytes, idesc_ts, h, j > 0 || h > 0);
                     }
+                    if (!ok) break;
                     ds_par ^= 1;
-                    tc_fence_after();
-                    // Q and dO are free once the last dP is done and the elementwise warps, which
-                    // read dO for Delta before their first dS, have arrived on ds_full.
-                    if (j + 1 == nkv) tc_commit(&bars->fixed_empty);
-                    issue_ts(tDQ, tS, sRing + ks * kTileBytes, idesc_ts, j > 0);      // dQ += dS K_j
                     tc_commit(&bars->ring_empty[ks]);
                     tc_commit(&bars->ring_empty[vs]);
                 }
@@ -329,91 +375,95 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait_bounded(&bars->mma_done, 0, &never, &g_fab_error_word, kErrDrain, 1000000000ull);
         }
     } else {
-        // ===================== elementwise: Delta, dS, dQ epilogue (row = thread) =====================
-        const uint32_t t = threadIdx.x;  // TMEM lane = row within the block
+        // ============ elementwise: Delta, dS, dQ epilogue (row = TMEM lane, warpgroup g = column half) ============
+        const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
         const uint8_t* tDOs = smem + kOffFixed + kTileBytes;
         uint32_t it = 0, sdp_par = 0, acc_par = 0;
+        bool ok = true;
         Units u(blockIdx.x);
         uint32_t bh, qb;
-        while (u.next(p, bh, qb)) {
+        while (ok && u.next(p, bh, qb)) {
             const uint32_t row = qb * kBlk + t;
             const bool valid = row < p.S_q;
             const size_t ridx = static_cast<size_t>(bh) * p.S_q + row;
-            bool ok = mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrElem);
-            if (!__all_sync(0xffffffffu, ok)) break;
+            ok = ew_all(mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrElem));
+            if (!ok) break;
             ++it;
-            // Delta = rowsum(dO * O) for this row (dO from the staged tile, O from global).
-            float delta = 0.f, lse2 = INFINITY;
+            // Delta = rowsum(dO * O): warpgroup g sums columns [64g, 64g+64) (dO from the staged
+            // tile, O from global), the halves meet in shared memory.
+            float part = 0.f, nlse2 = -INFINITY;
             if (valid) {
                 const uint4* orow = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.o) + ridx * 128);
 #pragma unroll 4
-                for (uint32_t c = 0; c < 16; ++c) {
+                for (uint32_t c = 8 * g; c < 8 * g + 8; ++c) {
                     const uint4 a = tile_chunk(tDOs, t, c), b = __ldg(orow + c);
                     const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const float2 x = unpack2<kBF16>(aw[e]), y = unpack2<kBF16>(bw[e]);
-                        delta = fmaf(x.x, y.x, fmaf(x.y, y.y, delta));
+                        part = fmaf(x.x, y.x, fmaf(x.y, y.y, part));
                     }
                 }
-                p.delta[ridx] = delta;
-                lse2 = p.lse[ridx] * 1.4426950408889634f;
+                nlse2 = -p.lse[ridx] * 1.4426950408889634f;
             }
+            s_part[g * kBlk + t] = part;
+            ew_sync();
+            const float delta = s_part[t] + s_part[kBlk + t];
+            if (valid && g == 0) p.delta[ridx] = delta;
             const uint32_t nkv = kv_blocks_for(p, qb);
-            for (uint32_t j = 0; j < nkv && ok; ++j) {
-                ok = mbar_wait_bounded(&bars->sdp_full, sdp_par, abort_flag, &g_fab_error_word, kErrElem);
-                if (!__all_sync(0xffffffffu, ok)) {
-                    ok = false;
-                    break;
-                }
+            for (uint32_t j = 0; j < nkv; ++j) {
+                ok = ew_all(mbar_wait_bounded(&bars->sdp_full, sdp_par, abort_flag, &g_fab_error_word, kErrElem));
+                if (!ok) break;
                 sdp_par ^= 1;
                 tc_fence_after();
-                // keys of this block visible from this row: causal (k <= row) and the key tail
-                int32_t lim = static_cast<int32_t>(p.S_k) - static_cast<int32_t>(j * kBlk);
-                if (p.causal) {
-                    const int32_t lc = static_cast<int32_t>(row) - static_cast<int32_t>(j * kBlk) + 1;
-                    if (lc < lim) lim = lc;
-                }
+                // the diagonal block masks keys past the row (top-left causal: key k <= row)
+                const int32_t lim = static_cast<int32_t>(t) + 1 - static_cast<int32_t>(64 * g);
+                auto ds_tile = [&](auto masked) {
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t s[32], dp[32], pk[16];
-                    tmem_ld32(tmem_base + c * 32 + lane_field, s);
-                    tmem_ld32(tmem_base + 128 + c * 32 + lane_field, dp);
-                    tmem_wait_ld();
+                    for (uint32_t c = 0; c < 2; ++c) {
+                        uint32_t s[32], dp[32], pk[16];
+                        tmem_ld32(tmem_base + 64 * g + 32 * c + lane_field, s);
+                        tmem_ld32(tmem_base + 128 + 64 * g + 32 * c + lane_field, dp);
+                        tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        float ds[2];
+                        for (int e = 0; e < 16; ++e) {
+                            float ds[2];
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int key = c * 32 + 2 * e + h;
-                            const float pr = key < lim ? ex2(__uint_as_float(s[2 * e + h]) * p.scale_log2 - lse2) : 0.f;
-                            ds[h] = pr * (__uint_as_float(dp[2 * e + h]) - delta);
+                            for (int h = 0; h < 2; ++h) {
+                                float pr = ex2(fmaf(__uint_as_float(s[2 * e + h]), p.scale_log2, nlse2));
+                                if (decltype(masked)::value && static_cast<int32_t>(32 * c) + 2 * e + h >= lim) pr = 0.f;
+                                ds[h] = pr * (__uint_as_float(dp[2 * e + h]) - delta);
+                            }
+                            pk[e] = pack2<kBF16>(ds[0], ds[1]);
                         }
-                        pk[e] = pack2<kBF16>(ds[0], ds[1]);
+                        tmem_st16(tmem_base + 64 * g + 16 * c + lane_field, pk);
                     }
-                    tmem_st16(tmem_base + c * 16 + lane_field, pk);
-                }
+                };
+                if (p.causal && j == qb)
+                    ds_tile(std::true_type{});
+                else
+                    ds_tile(std::false_type{});
                 tmem_wait_st();
                 tc_fence_before();
-                mbar_arrive(&bars->ds_full);
+                mbar_arrive(&bars->ds_half[g]);
             }
             if (!ok) break;
-            ok = mbar_wait_bounded(&bars->acc_full, acc_par, abort_flag, &g_fab_error_word, kErrElem);
-            if (!__all_sync(0xffffffffu, ok)) break;
+            ok = ew_all(mbar_wait_bounded(&bars->acc_full, acc_par, abort_flag, &g_fab_error_word, kErrElem));
+            if (!ok) break;
             acc_par ^= 1;
             tc_fence_after();
             uint8_t* dq_row = static_cast<uint8_t*>(p.out0) + ridx * 128 * 2;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (uint32_t c = 0; c < 2; ++c) {
                 uint32_t acc[32], pk[16];
-                tmem_ld32(tmem_base + 256 + c * 32 + lane_field, acc);
+                tmem_ld32(tmem_base + 256 + 64 * g + 32 * c + lane_field, acc);
                 tmem_wait_ld();
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
                     pk[e] = pack2<kBF16>(__uint_as_float(acc[2 * e]) * p.scale, __uint_as_float(acc[2 * e + 1]) * p.scale);
                 if (valid) {
-                    uint4* dst = reinterpret_cast<uint4*>(dq_row + c * 64);
+                    uint4* dst = reinterpret_cast<uint4*>(dq_row + (64 * g + 32 * c) * 2);
 #pragma unroll
                     for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
                 }
@@ -421,13 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
         }
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (warp == 4) {
-        __syncwarp();
-        tmem_dealloc(tmem_base, 512);
-    }
+    teardown_cta(tmem_base, warp);
 }
 
 // ============================================================================================
@@ -443,37 +487,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + sizeof(Bars));
     volatile uint32_t* abort_flag = tmem_slot + 1;
-    float* s_lse = reinterpret_cast<float*>(smem + kOffVec);
-    float* s_delta = s_lse + kBlk;
+    // per query block, double-buffered: [buf][0][128] = -lse * log2(e), [buf][1][128] = Delta
+    float* s_vec = reinterpret_cast<float*>(smem + kOffVec);
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const uint32_t nq = n_blocks(p.S_q);
-    if (threadIdx.x == 0) {
-        mbar_init(&bars->fixed_full, 1);
-        mbar_init(&bars->fixed_empty, 1);
-        for (uint32_t s = 0; s < kStages; ++s) {
-            mbar_init(&bars->ring_full[s], 1);
-            mbar_init(&bars->ring_empty[s], 1);
-        }
-        mbar_init(&bars->sdp_full, 1);
-        mbar_init(&bars->ds_full, 128);
-        mbar_init(&bars->acc_full, 1);
-        mbar_init(&bars->mma_done, 1);
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    if (warp == 4) {
-        tmem_alloc(tmem_slot, 512);
-        tmem_relinquish();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
+    const uint32_t tmem_base = setup_cta(bars, tmem_slot, abort_flag, warp);
     const uint32_t sK = smem_u32(smem + kOffFixed), sV = sK + kTileBytes, sRing = smem_u32(smem + kOffRing);
-    // TMEM: S^T [0,128), dP^T [128,256), dV [256,384), dK [384,512); P^T over S^T, dS^T over dP^T.
-    if (warp == 5) {
+    // TMEM: S^T [0,128), dP^T [128,256), dV [256,384), dK [384,512); warpgroup g packs its half of
+    // P^T / dS^T into columns [64g, 64g+32) of S^T / dP^T.
+    if (warp == kTmaWarp) {
         if (lane == 0) {
-            uint32_t stage = 0, phase = 0, it = 0, pend_valid = 0, pend_phase = 0;
+            Ring ring;
+            uint32_t it = 0;
             int32_t fixed_pending = -1;
             bool ok = true;
             Units u(blockIdx.x);
@@ -493,55 +518,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 fixed_pending = static_cast<int32_t>(it & 1);
                 ++it;
-                for (uint32_t i = q0; i < nq && ok; ++i) {
-                    for (uint32_t x = 0; x < 2; ++x) {  // Q_i, then dO_i
-                        if (!mbar_wait_bounded(&bars->ring_empty[stage], phase ^ 1, abort_flag, &g_fab_error_word,
-                                               kErrProducer)) {
-                            ok = false;
-                            break;
-                        }
-                        mbar_arrive_expect_tx(&bars->ring_full[stage], kTileBytes);
-                        for (uint32_t h = 0; h < 2; ++h)
-                            tma_load_3d(smem + kOffRing + stage * kTileBytes + h * kPanelBytes, x ? &tm_do : &tm_q,
-                                        &bars->ring_full[stage], h * 64, i * kBlk, bh);
-                        pend_valid |= 1u << stage;
-                        pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
-                        if (++stage == kStages) {
-                            stage = 0;
-                            phase ^= 1;
-                        }
-                    }
-                }
+                for (uint32_t i = q0; i < nq && ok; ++i)  // Q_i, then dO_i
+                    ok = ring.load(bars, smem, &tm_q, i, bh, abort_flag) && ring.load(bars, smem, &tm_do, i, bh, abort_flag);
             }
-            if (!ok) {
-                volatile uint32_t never = 0;
-                for (uint32_t s = 0; s < kStages; ++s)
-                    if (pend_valid & (1u << s))
-                        mbar_wait_bounded(&bars->ring_full[s], (pend_phase >> s) & 1u, &never, &g_fab_error_word,
-                                          kErrDrain, 1000000000ull);
-                if (fixed_pending >= 0)
-                    mbar_wait_bounded(&bars->fixed_full, static_cast<uint32_t>(fixed_pending), &never,
-                                      &g_fab_error_word, kErrDrain, 1000000000ull);
-            }
+            if (!ok) ring.drain(bars, fixed_pending);
         }
-    } else if (warp == 4) {
+    } else if (warp == kMmaWarp) {
         if (lane == 0) {
             const uint32_t idesc_ss = make_idesc_f16(kBF16, 128, 128, false, false);
             const uint32_t idesc_ts = make_idesc_f16(kBF16, 128, 128, false, true);
             const uint32_t tS = tmem_base, tDP = tmem_base + 128, tDV = tmem_base + 256, tDK = tmem_base + 384;
-            uint32_t stage = 0, phase = 0, it = 0, ds_par = 0;
+            RingWait ring;
+            uint32_t it = 0, ds_par = 0;
             bool ok = true;
-            auto wait_ring = [&](uint32_t& st) -> bool {
-                if (!mbar_wait_bounded(&bars->ring_full[stage], phase, abort_flag, &g_fab_error_word, kErrMma))
-                    return false;
-                tc_fence_after();
-                st = stage;
-                if (++stage == kStages) {
-                    stage = 0;
-                    phase ^= 1;
-                }
-                return true;
-            };
             Units u(blockIdx.x);
             uint32_t bh, kb;
             while (ok && u.next(p, bh, kb)) {
@@ -555,19 +544,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 for (uint32_t i = q0; i < nq; ++i) {
                     uint32_t qs, os;
-                    if (!wait_ring(qs)) { ok = false; break; }
+                    if (!ring.next(bars, abort_flag, qs)) { ok = false; break; }
                     issue_ss(tS, sK, sRing + qs * kTileBytes, idesc_ss);              // S^T = K Q_i^T
-                    if (!wait_ring(os)) { ok = false; break; }
+                    if (!ring.next(bars, abort_flag, os)) { ok = false; break; }
                     issue_ss(tDP, sV, sRing + os * kTileBytes, idesc_ss);             // dP^T = V dO_i^T
                     tc_commit(&bars->sdp_full);
-                    if (!mbar_wait_bounded(&bars->ds_full, ds_par, abort_flag, &g_fab_error_word, kErrMma)) {
-                        ok = false;
-                        break;
+                    for (uint32_t h = 0; h < 2 && ok; ++h) {                         // by query halves
+                        if (!mbar_wait_bounded(&bars->ds_half[h], ds_par, abort_flag, &g_fab_error_word, kErrMma)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const bool acc = i > q0 || h > 0;
+                        issue_ts_half(tDV, tS, sRing + os * kTileBytes, idesc_ts, h, acc);   // dV += P^T dO_i
+                        issue_ts_half(tDK, tDP, sRing + qs * kTileBytes, idesc_ts, h, acc);  // dK += dS^T Q_i
                     }
+                    if (!ok) break;
                     ds_par ^= 1;
-                    tc_fence_after();
-                    issue_ts(tDV, tS, sRing + os * kTileBytes, idesc_ts, i > q0);     // dV += P^T dO_i
-                    issue_ts(tDK, tDP, sRing + qs * kTileBytes, idesc_ts, i > q0);    // dK += dS^T Q_i
                     tc_commit(&bars->ring_empty[qs]);
                     tc_commit(&bars->ring_empty[os]);
                 }
@@ -580,10 +573,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait_bounded(&bars->mma_done, 0, &never, &g_fab_error_word, kErrDrain, 1000000000ull);
         }
     } else {
-        // =================== elementwise: P^T, dS^T, dK/dV epilogue (key = thread) ===================
-        const uint32_t t = threadIdx.x;  // TMEM lane = key within the block
+        // ====== elementwise: P^T, dS^T, dK/dV epilogue (key = TMEM lane, warpgroup g = query half) ======
+        const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
-        uint32_t sdp_par = 0, acc_par = 0;
+        uint32_t sdp_par = 0, acc_par = 0, nblk = 0;
         Units u(blockIdx.x);
         uint32_t bh, kb;
         bool ok = true;
@@ -592,61 +585,78 @@ __global__ void __launch_bounds__(kThreads, 1)
             const size_t kidx = static_cast<size_t>(bh) * p.S_k + key;
             const uint32_t q0 = q_first_for(p, kb);
             if (q0 < nq) {
-                for (uint32_t i = q0; i < nq; ++i) {
-                    // stage lse (log2 domain; +inf for rows past S_q, so their P is 0) and Delta of block i
-                    wg_sync();  // every thread is done reading the previous block's values
+                for (uint32_t i = q0; i < nq; ++i, ++nblk) {
+                    // stage -lse*log2(e) (-inf past S_q, so P = 0 there) and Delta of block i.  Buffer
+                    // nblk & 1 was last read two blocks ago, before every thread passed the previous
+                    // block's barrier, which this thread has passed too.
+                    float* vec = s_vec + (nblk & 1) * 2 * kBlk;
                     const uint32_t r = i * kBlk + t;
                     const size_t ridx = static_cast<size_t>(bh) * p.S_q + r;
-                    s_lse[t] = r < p.S_q ? p.lse[ridx] * 1.4426950408889634f : INFINITY;
-                    s_delta[t] = r < p.S_q ? p.delta[ridx] : 0.f;
+                    if (g == 0)
+                        vec[t] = r < p.S_q ? -p.lse[ridx] * 1.4426950408889634f : -INFINITY;
+                    else
+                        vec[kBlk + t] = r < p.S_q ? p.delta[ridx] : 0.f;
                     // publishes the staged values and makes the give-up decision uniform
-                    ok = wg_all(mbar_wait_bounded(&bars->sdp_full, sdp_par, abort_flag, &g_fab_error_word, kErrElem));
+                    ok = ew_all(mbar_wait_bounded(&bars->sdp_full, sdp_par, abort_flag, &g_fab_error_word, kErrElem));
                     if (!ok) break;
                     sdp_par ^= 1;
                     tc_fence_after();
-                    // rows of block i that see this key: causal (key <= row), i.e. row index >= first
-                    const int32_t first = p.causal ? static_cast<int32_t>(key) - static_cast<int32_t>(i * kBlk) : 0;
+                    // on the diagonal block, query column q sees this key when q >= t (key <= row)
+                    const int32_t first = static_cast<int32_t>(t) - static_cast<int32_t>(64 * g);
+                    auto pds_tile = [&](auto masked) {
 #pragma unroll 1
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t s[32], dp[32], pp[16], pd[16];
-                        tmem_ld32(tmem_base + c * 32 + lane_field, s);
-                        tmem_ld32(tmem_base + 128 + c * 32 + lane_field, dp);
-                        tmem_wait_ld();
+                        for (uint32_t c = 0; c < 2; ++c) {
+                            uint32_t s[32], dp[32], pp[16], pd[16];
+                            tmem_ld32(tmem_base + 64 * g + 32 * c + lane_field, s);
+                            tmem_ld32(tmem_base + 128 + 64 * g + 32 * c + lane_field, dp);
+                            const float4* nl4 = reinterpret_cast<const float4*>(vec + 64 * g + 32 * c);
+                            const float4* dl4 = reinterpret_cast<const float4*>(vec + kBlk + 64 * g + 32 * c);
+                            tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            float pr[2], ds[2];
+                            for (int e4 = 0; e4 < 8; ++e4) {
+                                const float4 nl = nl4[e4], dl = dl4[e4];
+                                const float nla[4] = {nl.x, nl.y, nl.z, nl.w}, dla[4] = {dl.x, dl.y, dl.z, dl.w};
+                                float pr[4], ds[4];
 #pragma unroll
-                            for (int h = 0; h < 2; ++h) {
-                                const int col = c * 32 + 2 * e + h;
-                                pr[h] = col >= first ? ex2(__uint_as_float(s[2 * e + h]) * p.scale_log2 - s_lse[col]) : 0.f;
-                                ds[h] = pr[h] * (__uint_as_float(dp[2 * e + h]) - s_delta[col]);
+                                for (int h = 0; h < 4; ++h) {
+                                    const int col = 4 * e4 + h;
+                                    pr[h] = ex2(fmaf(__uint_as_float(s[col]), p.scale_log2, nla[h]));
+                                    if (decltype(masked)::value && static_cast<int32_t>(32 * c) + col < first) pr[h] = 0.f;
+                                    ds[h] = pr[h] * (__uint_as_float(dp[col]) - dla[h]);
+                                }
+                                pp[2 * e4] = pack2<kBF16>(pr[0], pr[1]);
+                                pp[2 * e4 + 1] = pack2<kBF16>(pr[2], pr[3]);
+                                pd[2 * e4] = pack2<kBF16>(ds[0], ds[1]);
+                                pd[2 * e4 + 1] = pack2<kBF16>(ds[2], ds[3]);
                             }
-                            pp[e] = pack2<kBF16>(pr[0], pr[1]);
-                            pd[e] = pack2<kBF16>(ds[0], ds[1]);
+                            tmem_st16(tmem_base + 64 * g + 16 * c + lane_field, pp);
+                            tmem_st16(tmem_base + 128 + 64 * g + 16 * c + lane_field, pd);
                         }
-                        tmem_st16(tmem_base + c * 16 + lane_field, pp);
-                        tmem_st16(tmem_base + 128 + c * 16 + lane_field, pd);
-                    }
+                    };
+                    if (p.causal && i == kb)
+                        pds_tile(std::true_type{});
+                    else
+                        pds_tile(std::false_type{});
                     tmem_wait_st();
                     tc_fence_before();
-                    mbar_arrive(&bars->ds_full);
+                    mbar_arrive(&bars->ds_half[g]);
                 }
                 if (!ok) break;
-                ok = wg_all(mbar_wait_bounded(&bars->acc_full, acc_par, abort_flag, &g_fab_error_word, kErrElem));
+                ok = ew_all(mbar_wait_bounded(&bars->acc_full, acc_par, abort_flag, &g_fab_error_word, kErrElem));
                 if (!ok) break;
                 acc_par ^= 1;
                 tc_fence_after();
             }
-            // epilogue: dV, dK (scaled) of this key; zeros when no query sees the block
+            // epilogue: dV, dK (scaled) of this key, columns [64g, 64g+64); zeros when no query sees the block
             const bool valid = key < p.S_k;
             uint8_t* dk_row = static_cast<uint8_t*>(p.out0) + kidx * 128 * 2;
             uint8_t* dv_row = static_cast<uint8_t*>(p.out1) + kidx * 128 * 2;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (uint32_t c = 0; c < 2; ++c) {
                 uint32_t av[32], ak[32], pv[16], pk[16];
                 if (q0 < nq) {
-                    tmem_ld32(tmem_base + 256 + c * 32 + lane_field, av);
-                    tmem_ld32(tmem_base + 384 + c * 32 + lane_field, ak);
+                    tmem_ld32(tmem_base + 256 + 64 * g + 32 * c + lane_field, av);
+                    tmem_ld32(tmem_base + 384 + 64 * g + 32 * c + lane_field, ak);
                     tmem_wait_ld();
                 } else {
 #pragma unroll
@@ -658,8 +668,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     pk[e] = pack2<kBF16>(__uint_as_float(ak[2 * e]) * p.scale, __uint_as_float(ak[2 * e + 1]) * p.scale);
                 }
                 if (valid) {
-                    uint4* dv = reinterpret_cast<uint4*>(dv_row + c * 64);
-                    uint4* dk = reinterpret_cast<uint4*>(dk_row + c * 64);
+                    uint4* dv = reinterpret_cast<uint4*>(dv_row + (64 * g + 32 * c) * 2);
+                    uint4* dk = reinterpret_cast<uint4*>(dk_row + (64 * g + 32 * c) * 2);
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
                         dv[v] = make_uint4(pv[4 * v], pv[4 * v + 1], pv[4 * v + 2], pv[4 * v + 3]);
@@ -670,13 +680,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
         }
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (warp == 4) {
-        __syncwarp();
-        tmem_dealloc(tmem_base, 512);
-    }
+    teardown_cta(tmem_base, warp);
 }
 
 // ============================================================================================

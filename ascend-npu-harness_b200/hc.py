@@ -339,10 +339,11 @@ def flash_attention_fwd(q, k, v, causal: bool, scale: float | None = None, with_
     return out, (lse if with_lse else None)
 
 
-def flash_attention_bwd(q, k, v, o, lse, dout, causal: bool, scale: float | None = None, stream=None):
+def flash_attention_bwd(q, k, v, o, lse, dout, causal: bool, scale: float | None = None, out=None, stream=None):
     """Gradients of O = softmax(Q K^T * scale [causal]) V for [B, H, S, D] tensors, from the forward's
     o and lse and the output gradient dout; returns (dq, dk, dv, delta) with delta = rowsum(dout * o)
-    fp32 [B, H, S_q].  K and V have H heads (no grouped-query form)."""
+    fp32 [B, H, S_q].  K and V have H heads (no grouped-query form).  `out` may give the four
+    output tensors (allocated otherwise)."""
     torch = _torch()
     B, H, S_q, D = q.shape
     S_k, D_v = k.shape[2], v.shape[3]
@@ -350,8 +351,10 @@ def flash_attention_bwd(q, k, v, o, lse, dout, causal: bool, scale: float | None
         raise HcError(HC_ERR_UNSUPPORTED, "flash_attention_bwd: K/V must have the query head count")
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    delta = torch.empty((B, H, S_q), dtype=torch.float32, device=q.device)
+    if out is None:
+        out = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
+               torch.empty((B, H, S_q), dtype=torch.float32, device=q.device))
+    dq, dk, dv, delta = out
     t = FlashAttentionFwdFusedTiling(B, H, S_q, S_k, D, D_v, scale, 1 if causal else 0)
     check(load().hc_flash_attention_bwd_launch(_ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dout), _ptr(lse), _ptr(dq),
                                                _ptr(dk), _ptr(dv), _ptr(delta), C.byref(t), dtype_code(q),

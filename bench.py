@@ -405,10 +405,50 @@ def check_fa_heads(q, k, v, o, lse, causal: bool, n_sample: int = 4) -> dict:
     return worst
 
 
+# Algorithmic FLOPs of the backward per visible (query, key) pair, as a multiple of the forward's
+# 4*D: five products of 2*D each (S recomputed, dP, dV, dK, dQ).  The tensor-core kernels issue
+# seven (S and dP are formed once for dQ and once for dK/dV); only the five count.
+FA_BWD_FLOP_RATIO = 2.5
+FA_BWD_TOL = 1e-2  # normwise ||got - exact|| / ||exact|| per gradient, bf16
+
+
+def check_fa_bwd_heads(q, k, v, dout, grads, causal: bool, n_sample: int = 2) -> dict:
+    """Sampled heads of the backward against fp32 gradients on the device (no TF32): dq, dk, dv
+    each within FA_BWD_TOL normwise; max_abs/max_rel report the worst element."""
+    import torch
+
+    h = q.shape[1]
+    heads = sorted({0, h - 1, *[int(i) for i in torch.linspace(0, h - 1, n_sample).round().tolist()]})
+    scale = 1.0 / math.sqrt(q.shape[-1])
+    worst = {"max_abs": 0.0, "max_rel": 0.0, "pass": True, "normwise": 0.0}
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for i in heads:
+            qf, kf, vf, df = (t[0, i].float() for t in (q, k, v, dout))
+            s = (qf @ kf.T) * scale
+            if causal:
+                s = s.masked_fill(torch.ones_like(s, dtype=torch.bool).triu(1), float("-inf"))
+            p = torch.softmax(s, dim=-1)
+            dp = df @ vf.T
+            ds = p * (dp - (p * dp).sum(-1, keepdim=True))
+            for ref, got in (((ds @ kf) * scale, grads[0][0, i]), ((ds.T @ qf) * scale, grads[1][0, i]),
+                             (p.T @ df, grads[2][0, i])):
+                acc = accuracy(ref, got, 0.0, 0.0)
+                nw = float((got.double() - ref.double()).norm() / ref.double().norm())
+                worst["max_abs"] = max(worst["max_abs"], acc["max_abs"])
+                worst["max_rel"] = max(worst["max_rel"], acc["max_rel"])
+                worst["normwise"] = max(worst["normwise"], nw)
+                worst["pass"] &= nw <= FA_BWD_TOL
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return worst
+
+
 def merge_acc(d: "Dist", acc: dict) -> dict:
     """Worst accuracy over the ranks (max of the errors, AND of the verdicts)."""
     out = dict(acc)
-    for key in ("max_abs", "max_rel", "lse_max_abs"):
+    for key in ("max_abs", "max_rel", "lse_max_abs", "normwise"):
         if key in acc:
             out[key] = d.max(acc[key])
     out["pass"] = d.max(0.0 if acc["pass"] else 1.0) == 0.0
@@ -580,12 +620,12 @@ def run_ours(args):
     d.close()
 
 
-EXTRA_OPS = ("flash_attention_fwd_noncausal", "matmul_bias", "layer_norm", "rms_norm_rope_fused", "elementwise_add",
+EXTRA_OPS = ("flash_attention_fwd_noncausal", "flash_attention_bwd", "matmul_bias", "layer_norm", "rms_norm_rope_fused", "elementwise_add",
              "axpy_scalar_affine", "broadcast_binary", "activation_gelu_silu", "reduce_sum_lastdim", "transpose_2d_4d")
 # The last five ops have no configuration of their own in the reference's benchmark list; they are
 # timed on sized analogs of the layer_norm shape (134 MB of 16-bit input per launch); the shapes
 # are listed in the design notes.
-ANALOG_OPS = EXTRA_OPS[5:]
+ANALOG_OPS = EXTRA_OPS[6:]
 
 
 def settle():
@@ -642,6 +682,8 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
             job = total_units * unit_bytes_or_flops / (ms * 1e-3) / 1e12
             e = {"value": job, "unit": "TFLOP/s", "frac": per / 1e12 / peaks["bf16_tflops"]}
         e.update({"ms": ms, "max_abs": acc["max_abs"], "max_rel": acc["max_rel"], "pass": acc["pass"]})
+        if "normwise" in acc:
+            e["normwise"] = acc["normwise"]
         out[name] = e
 
     if "flash_attention_fwd_noncausal" in want:  # same shapes as the headline, no mask
@@ -655,6 +697,21 @@ def run_extras(hc, d: Dist, dev, peaks, args, want=EXTRA_OPS) -> dict:
         acc = check_fa_heads(q, k, v, o, lse, False, n_sample=2)
         entry("flash_attention_fwd_noncausal", total, hn, fa_flops(1, 1, FA_S, FA_S, FA_D, False), ms, acc, "tensor")
         del q, k, v, o, lse
+
+    if "flash_attention_bwd" in want:  # backward of the headline (same shapes, causal)
+        total = args.fa_batch * FA_H
+        _, hn = shard_range(total, n, r)
+        q, k, v = fa_inputs(dev, hn, 70 + 3 * r)
+        dout = fa_inputs(dev, hn, 80 + 3 * r)[0]
+        o, lse = hc.flash_attention_fwd(q, k, v, True)
+        grads = (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(lse))
+        settle()
+        ms = time_launches(lambda: hc.flash_attention_bwd(q, k, v, o, lse, dout, True, out=grads), 5, warm, d,
+                           local=True)
+        acc = check_fa_bwd_heads(q, k, v, dout, grads, True)
+        entry("flash_attention_bwd", total, hn, FA_BWD_FLOP_RATIO * fa_flops(1, 1, FA_S, FA_S, FA_D, True), ms, acc,
+              "tensor")
+        del q, k, v, dout, o, lse, grads
 
     if "matmul_bias" in want:  # 8192^3 bf16, M rows split over the ranks, B replicated
         cfg = specs.bench_config("matmul_bias")

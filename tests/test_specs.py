@@ -99,4 +99,5 @@ def test_bench_reads_the_specs():
     fa = specs.bench_config("flash_attention_fwd_fused")
     assert (bench.FA_B, bench.FA_H, bench.FA_S, bench.FA_D) == (fa["B"], fa["H"], fa["S_q"], fa["D"])
     assert bench.FA_TOL == specs.tolerance("flash_attention_fwd_fused", "bfloat16")
-    assert set(bench.EXTRA_OPS) == {"flash_attention_fwd_noncausal", *OPS} - {"flash_attention_fwd_fused"}
+    assert set(bench.EXTRA_OPS) == {"flash_attention_fwd_noncausal", "flash_attention_bwd", *OPS} - \
+        {"flash_attention_fwd_fused"}
