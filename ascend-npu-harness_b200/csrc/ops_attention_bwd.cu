@@ -4,27 +4,35 @@
 //   P = exp(S * scale - lse), dV = P^T dO, dP = dO V^T, Delta = rowsum(dO * O),
 //   dS = P * (dP - Delta), dQ = scale * dS K, dK = scale * dS^T Q.
 //
-// Tensor-core path (bf16/fp16, D = D_v = 128, 16-byte aligned buffers), two kernels that reuse the
-// forward's operand forms (SS Q K^T-style products with both operands K-major, TS products with
-// the 16-bit operand read from TMEM and an MN-major shared-memory operand):
-//   * fa_bwd_dq_kernel: a CTA per 128-row query block (rows on TMEM lanes).  It first computes
-//     Delta for its rows (dO from shared memory, O from global), then for every visible 128-key
-//     block j: S = Q K_j^T and dP = dO V_j^T into TMEM, dS (16-bit) over S, dQ += dS K_j.
-//     It writes dQ and Delta (the [B, H, S_q] fp32 buffer the caller provides).
-//   * fa_bwd_dkdv_kernel: a CTA per 128-key block (keys on TMEM lanes), launched after the dQ
-//     kernel: for every query block i that sees the keys: S^T = K Q_i^T and dP^T = V dO_i^T,
-//     P^T and dS^T (16-bit) over them, dV += P^T dO_i and dK += dS^T Q_i, accumulated in TMEM
-//     (S^T, dP^T, dV, dK = 512 columns) and written once at the end.
-// Roles per CTA: two elementwise warpgroups (warps 0-3 and 4-7; a thread owns one TMEM lane, i.e.
-// one row or key, and warpgroup g the 64 columns [64g, 64g+64) of every 128-column tile), warp 8
-// issues tcgen05.mma, warp 9 issues TMA (no multicast).  Each warpgroup writes its 16-bit half of
-// P / dS into its own columns, and the MMA warp issues the TMEM-operand products half by half (K
-// steps 0-3 after warpgroup 0, 4-7 after warpgroup 1).  The causal mask is applied only on the
-// diagonal block; tails need none (rows past S_q get lse = +inf, so P = 0; keys past S_k only
-// reach accumulator rows that are not stored, or meet zero K/V rows).  Work units are handed out
-// as complementary block pairs (b, n-1-b) of one head so that every CTA gets the same causal work.
-// Every mbarrier wait is bounded as in the forward kernel, and the two warpgroups take every
-// give-up decision together (a barrier that ANDs their results), so none is left at a barrier.
+// Tensor-core path (bf16/fp16, D = D_v = 128, 16-byte aligned buffers): two kernels with the same
+// structure.  A CTA holds two 128 x 128 "fixed" tiles of one 128-row block in shared memory and
+// streams the other side's 128-row tiles through a 4-stage TMA ring (two blocks in flight):
+//   * fa_bwd_dq_kernel: fixed Q, dO of a query block (rows on TMEM lanes); for every visible key
+//     block j: S = Q K_j^T, dP = dO V_j^T, dS = P (dP - Delta) (16-bit), dQ += dS K_j.  It first
+//     computes Delta = rowsum(dO * O) for its rows and writes it (the caller's [B, H, S_q] fp32
+//     buffer).  TMEM: S [0,128), dP [128,256) (dS packed over it), dQ [256,384).
+//   * fa_bwd_dkdv_kernel (launched after, it reads Delta): fixed K, V of a key block (keys on
+//     TMEM lanes); for every query block i that sees the keys: S^T = K Q_i^T, dP^T = V dO_i^T,
+//     P^T (16-bit, over S^T), dS^T (16-bit, over dP^T), dV += P^T dO_i, dK += dS^T Q_i.
+//     TMEM: S^T [0,128), dP^T [128,256), dV [256,384), dK [384,512).
+// Every product is M=128, N=128, K=16 per instruction: one tcgen05.mma every 64 cycles at the full
+// tensor rate (N = 64 runs at two thirds of it, bound by shared-memory operand reads).  The two
+// elementwise warpgroups (warps 0-3 and 4-7; a thread owns one TMEM lane, warpgroup g the 64 columns
+// [64g, 64g+64) of each tile) work in two phases per block, each with its own hand-off to the MMA
+// warp (warp 8), which keeps the tensor pipe busy during both:
+//   dQ:    phase 1 loads S and releases it (s_free; the next S is issued at once), forms P in
+//          registers; phase 2 forms dS from dP and packs it over dP (ds_full): dQ += dS K_j, then
+//          the next dP.
+//   dK/dV: phase 1 forms P^T from S^T and packs it over S^T (p_full): dV += P^T dO_i, then the next
+//          S^T; phase 2 forms dS^T and packs it over dP^T (ds_full): dK += dS^T Q_i, then the next
+//          dP^T.
+// The accumulators of the next work unit are started only after both warpgroups' epilogues have
+// read them (acc_empty).  Warp 9 issues TMA (no multicast).  The causal mask is applied only on the
+// diagonal block; tails need none (rows past S_q get lse = +inf, so P = 0; keys past S_k meet zero
+// K/V rows or land in accumulator rows that are not stored).  Work units are handed out as
+// complementary block pairs (b, n-1-b) of one head so that every CTA gets the same causal work.
+// Every mbarrier wait is bounded as in the forward kernel, and the threads of a warpgroup take
+// each give-up decision together (a barrier that ANDs their results), so none is left at a barrier.
 //
 // SIMT path: fp32, or any other head dims (<= 256): a warp per query row for dQ/Delta and a
 // warp per key row for dK/dV, fp32 math.
@@ -50,15 +58,15 @@ using namespace sm100;
 constexpr uint32_t kBlk = 128;                  // rows (queries or keys) per block
 constexpr uint32_t kPanelBytes = 128 * 64 * 2;  // one 64-column swizzle panel of a 128-row tile: 16 KB
 constexpr uint32_t kTileBytes = 2 * kPanelBytes;  // a 128 x 128 16-bit tile: 32 KB
-constexpr uint32_t kElemThreads = 256;          // two elementwise warpgroups
+constexpr uint32_t kHalf = 64;                  // columns of a tile per elementwise warpgroup
 constexpr uint32_t kMmaWarp = 8, kTmaWarp = 9;
-constexpr uint32_t kThreads = 320;
-constexpr uint32_t kStages = 4;                 // streamed-tile ring
+constexpr uint32_t kThreads = 320;              // two elementwise warpgroups, the MMA warp, the TMA warp
+constexpr uint32_t kStages = 4;                 // streamed-tile ring: two blocks of two tiles
 constexpr uint32_t kOffFixed = 0;               // two tiles resident per unit (Q,dO or K,V)
 constexpr uint32_t kOffRing = 2 * kTileBytes;
 constexpr uint32_t kOffBar = kOffRing + kStages * kTileBytes;
-constexpr uint32_t kOffVec = kOffBar + 256;     // dQ: Delta halves; dK/dV: -lse*log2(e) and Delta, double-buffered
-constexpr uint32_t kVecBytes = 2 * 2 * kBlk * 4;
+constexpr uint32_t kOffVec = kOffBar + 256;     // dK/dV: per warpgroup, double-buffered -lse*log2(e) and Delta
+constexpr uint32_t kVecBytes = 2 * 2 * 2 * kHalf * 4;
 constexpr uint32_t kSmemBytes = kOffVec + kVecBytes + 1024;
 
 enum : uint32_t {
@@ -83,7 +91,9 @@ struct Params {
 struct Bars {
     uint64_t fixed_full, fixed_empty;
     uint64_t ring_full[kStages], ring_empty[kStages];
-    uint64_t sdp_full, ds_half[2], acc_full;
+    uint64_t s_full, dp_full;      // MMA -> elementwise: S (S^T) and dP (dP^T) of the block are in TMEM
+    uint64_t mid, ds_full;         // elementwise -> MMA (256 arrivals): phase 1 done (dQ: S read; dK/dV: P^T packed), phase 2 (dS packed)
+    uint64_t acc_full, acc_empty;
     uint64_t mma_done;
 };
 
@@ -145,17 +155,16 @@ __device__ __forceinline__ void issue_ss(uint32_t d_tmem, uint32_t a_addr, uint3
     }
 }
 
-// Half h of D (M=128, N=128) (+)= A * B over K: A is the 16-bit tile in TMEM whose K range
-// [64h, 64h+64) sits in columns [64h, 64h+32) of `a_tmem` (each warpgroup packs its half of P or dS
-// into its own columns); B holds K rows [64h, 64h+64) of a 128-row MN-major smem tile.  K-steps
-// 4h..4h+3; `accumulate` false only for the first half of a fresh accumulator.
-__device__ __forceinline__ void issue_ts_half(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, uint32_t idesc,
-                                              uint32_t h, bool accumulate) {
+// D (M=128, N=128) (+)= A * B with B a 128-row MN-major smem tile (K along its rows) and A a 128 x 128
+// 16-bit tile in TMEM packed by the two warpgroups: K range [64g, 64g+64) in columns [64g, 64g+32)
+// from `a_tmem`.  `accumulate` false starts D afresh.
+__device__ __forceinline__ void issue_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, uint32_t idesc,
+                                         bool accumulate) {
     const Sw128Desc bd = make_sw128_desc2(b_addr, kPanelBytes, 1024);
 #pragma unroll
-    for (uint32_t s = 0; s < 4; ++s)
-        mma_ts2(d_tmem, a_tmem + h * 64 + s * 8, Sw128Desc{bd.lo + (4 * h + s) * (2048 >> 4), bd.hi}, idesc,
-                (accumulate || s > 0) ? 1u : 0u);
+    for (uint32_t kk = 0; kk < 8; ++kk)
+        mma_ts2(d_tmem, a_tmem + (kk >> 2) * kHalf + (kk & 3) * 8, Sw128Desc{bd.lo + kk * (2048 >> 4), bd.hi}, idesc,
+                (accumulate || kk > 0) ? 1u : 0u);
 }
 
 __device__ __forceinline__ uint32_t n_blocks(uint32_t S) { return (S + kBlk - 1) / kBlk; }
@@ -180,25 +189,23 @@ __device__ __forceinline__ uint4 tile_chunk(const uint8_t* tile, uint32_t row, u
     return *reinterpret_cast<const uint4*>(tile + (c >> 3) * kPanelBytes + row * 128 + (((c & 7) ^ (row & 7)) << 4));
 }
 
-// Barrier among the 256 elementwise threads only (named barrier 1).
-__device__ __forceinline__ void ew_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-
-// The same barrier, returning the AND of `pred` over both warpgroups: every warp takes the same
-// branch after it, so no warp can leave a loop that still has a barrier another warp waits on.
-__device__ __forceinline__ bool ew_all(bool pred) {
+// Barrier among the 128 threads of warpgroup g (named barrier 2 + g), returning the AND of `pred`
+// over them: the warpgroup takes the same branch after it, so no warp can leave a loop that still
+// has a barrier another warp of the group waits on.
+__device__ __forceinline__ bool wg_all(uint32_t g, bool pred) {
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.and.pred q, 1, 256, p;\n\t"
+        "bar.red.and.pred q, %2, 128, p;\n\t"
         "selp.u32 %0, 1, 0, q;\n\t}"
         : "=r"(r)
-        : "r"(static_cast<uint32_t>(pred))
+        : "r"(static_cast<uint32_t>(pred)), "r"(2 + g)
         : "memory");
     return r != 0;
 }
 
-// Shared setup of both kernels: barriers, TMEM (512 columns, warp 8), and the bounded-wait state.
+// Shared setup of both kernels: barriers, TMEM (512 columns, MMA warp), and the bounded-wait state.
 __device__ __forceinline__ uint32_t setup_cta(Bars* bars, uint32_t* tmem_slot, volatile uint32_t* abort_flag,
                                               uint32_t warp) {
     if (threadIdx.x == 0) {
@@ -208,10 +215,12 @@ __device__ __forceinline__ uint32_t setup_cta(Bars* bars, uint32_t* tmem_slot, v
             mbar_init(&bars->ring_full[s], 1);
             mbar_init(&bars->ring_empty[s], 1);
         }
-        mbar_init(&bars->sdp_full, 1);
-        mbar_init(&bars->ds_half[0], 128);
-        mbar_init(&bars->ds_half[1], 128);
+        mbar_init(&bars->s_full, 1);
+        mbar_init(&bars->dp_full, 1);
+        mbar_init(&bars->mid, 256);
+        mbar_init(&bars->ds_full, 256);
         mbar_init(&bars->acc_full, 1);
+        mbar_init(&bars->acc_empty, 256);
         mbar_init(&bars->mma_done, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -268,12 +277,11 @@ struct Ring {
     }
 };
 
-// The MMA warp's consumer side of the ring.
+// The MMA warp's consumer side of the ring: the next block's two streamed tiles.
 struct RingWait {
     uint32_t stage = 0, phase = 0;
-    __device__ __forceinline__ bool next(Bars* bars, volatile uint32_t* abort_flag, uint32_t& st) {
+    __device__ __forceinline__ bool one(Bars* bars, volatile uint32_t* abort_flag, uint32_t& st) {
         if (!mbar_wait_bounded(&bars->ring_full[stage], phase, abort_flag, &g_fab_error_word, kErrMma)) return false;
-        tc_fence_after();
         st = stage;
         if (++stage == kStages) {
             stage = 0;
@@ -281,7 +289,43 @@ struct RingWait {
         }
         return true;
     }
+    __device__ __forceinline__ bool pair(Bars* bars, volatile uint32_t* abort_flag, uint32_t& x, uint32_t& y) {
+        const bool ok = one(bars, abort_flag, x) && one(bars, abort_flag, y);
+        tc_fence_after();
+        return ok;
+    }
 };
+
+// Per-thread parities of the MMA warp's waits, kept across units.
+struct MmaPar {
+    uint32_t mid = 0, ds = 0;
+};
+
+__device__ __forceinline__ bool mma_wait(uint64_t* bar, uint32_t& par, volatile uint32_t* abort_flag) {
+    if (!mbar_wait_bounded(bar, par, abort_flag, &g_fab_error_word, kErrMma)) return false;
+    par ^= 1;
+    tc_fence_after();
+    return true;
+}
+
+__device__ __forceinline__ void mma_finish(Bars* bars) {
+    tc_commit(&bars->mma_done);
+    volatile uint32_t never = 0;
+    mbar_wait_bounded(&bars->mma_done, 0, &never, &g_fab_error_word, kErrDrain, 1000000000ull);
+}
+
+// Elementwise side: waits on an MMA barrier, decided for the whole warpgroup.
+__device__ __forceinline__ bool ew_wait(uint32_t g, uint64_t* bar, uint32_t& par, volatile uint32_t* abort_flag) {
+    if (!wg_all(g, mbar_wait_bounded(bar, par, abort_flag, &g_fab_error_word, kErrElem))) return false;
+    par ^= 1;
+    tc_fence_after();
+    return true;
+}
+
+__device__ __forceinline__ void ew_arrive(uint64_t* bar) {
+    tc_fence_before();
+    mbar_arrive(bar);
+}
 
 // ============================================================================================
 // dQ (and Delta)
@@ -296,11 +340,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + sizeof(Bars));
     volatile uint32_t* abort_flag = tmem_slot + 1;
-    float* s_part = reinterpret_cast<float*>(smem + kOffVec);  // [2][128] Delta halves
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const uint32_t tmem_base = setup_cta(bars, tmem_slot, abort_flag, warp);
     const uint32_t sQ = smem_u32(smem + kOffFixed), sDO = sQ + kTileBytes, sRing = smem_u32(smem + kOffRing);
-    // TMEM: S [0,128), dP [128,256), dQ [256,384); dS (16-bit) of warpgroup g in S columns [64g, 64g+32).
+    const uint32_t tS = tmem_base, tDP = tmem_base + 128, tDQ = tmem_base + 256;
     if (warp == kTmaWarp) {
         if (lane == 0) {
             Ring ring;
@@ -331,55 +374,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t idesc_ss = make_idesc_f16(kBF16, 128, 128, false, false);
             const uint32_t idesc_ts = make_idesc_f16(kBF16, 128, 128, false, true);
-            const uint32_t tS = tmem_base, tDP = tmem_base + 128, tDQ = tmem_base + 256;
             RingWait ring;
-            uint32_t it = 0, ds_par = 0;
-            bool ok = true;
+            MmaPar par;
+            uint32_t it = 0;
             Units u(blockIdx.x);
             uint32_t bh, qb;
-            for (; ok && u.next(p, bh, qb); ++it) {
-                if (!mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrMma)) {
-                    ok = false;
-                    break;
-                }
+            for (; u.next(p, bh, qb); ++it) {
+                const uint32_t n = kv_blocks_for(p, qb);
+                if (!mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrMma)) break;
                 tc_fence_after();
-                const uint32_t nkv = kv_blocks_for(p, qb);
-                for (uint32_t j = 0; j < nkv; ++j) {
-                    uint32_t ks, vs;
-                    if (!ring.next(bars, abort_flag, ks)) { ok = false; break; }
-                    issue_ss(tS, sQ, sRing + ks * kTileBytes, idesc_ss);              // S = Q K_j^T
-                    if (!ring.next(bars, abort_flag, vs)) { ok = false; break; }
-                    issue_ss(tDP, sDO, sRing + vs * kTileBytes, idesc_ss);            // dP = dO V_j^T
-                    tc_commit(&bars->sdp_full);
-                    for (uint32_t h = 0; h < 2 && ok; ++h) {                         // dQ += dS K_j, by key halves
-                        if (!mbar_wait_bounded(&bars->ds_half[h], ds_par, abort_flag, &g_fab_error_word, kErrMma)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        // Q and dO are free once the last dP is done and both warpgroups, which read
-                        // dO for Delta before their first dS, have arrived.
-                        if (h == 1 && j + 1 == nkv) tc_commit(&bars->fixed_empty);
-                        issue_ts_half(tDQ, tS, sRing + ks * kTileBytes, idesc_ts, h, j > 0 || h > 0);
+                uint32_t ks, vs;
+                if (!ring.pair(bars, abort_flag, ks, vs)) break;
+                issue_ss(tS, sQ, sRing + ks * kTileBytes, idesc_ss);             // S_0 = Q K_0^T
+                tc_commit(&bars->s_full);
+                issue_ss(tDP, sDO, sRing + vs * kTileBytes, idesc_ss);           // dP_0 = dO V_0^T
+                tc_commit(&bars->dp_full);
+                if (!mbar_wait_bounded(&bars->acc_empty, (it & 1) ^ 1, abort_flag, &g_fab_error_word, kErrMma)) break;
+                bool ok = true;
+                for (uint32_t j = 0; j < n && ok; ++j) {
+                    const bool nxt = j + 1 < n;
+                    uint32_t kn = 0, vn = 0;
+                    // S_j has been read into registers: the next S goes into its columns
+                    if (!mma_wait(&bars->mid, par.mid, abort_flag)) { ok = false; break; }
+                    if (nxt) {
+                        if (!ring.pair(bars, abort_flag, kn, vn)) { ok = false; break; }
+                        issue_ss(tS, sQ, sRing + kn * kTileBytes, idesc_ss);
+                        tc_commit(&bars->s_full);
                     }
-                    if (!ok) break;
-                    ds_par ^= 1;
+                    // dS_j packed over dP_j: dQ += dS_j K_j, then the next dP into those columns
+                    if (!mma_wait(&bars->ds_full, par.ds, abort_flag)) { ok = false; break; }
+                    issue_ts(tDQ, tDP, sRing + ks * kTileBytes, idesc_ts, j > 0);
+                    if (nxt) {
+                        issue_ss(tDP, sDO, sRing + vn * kTileBytes, idesc_ss);
+                        tc_commit(&bars->dp_full);
+                    }
                     tc_commit(&bars->ring_empty[ks]);
                     tc_commit(&bars->ring_empty[vs]);
+                    ks = kn;
+                    vs = vn;
                 }
                 if (!ok) break;
+                tc_commit(&bars->fixed_empty);
                 tc_commit(&bars->acc_full);
             }
-            tc_commit(&bars->mma_done);
-            volatile uint32_t never = 0;
-            mbar_wait_bounded(&bars->mma_done, 0, &never, &g_fab_error_word, kErrDrain, 1000000000ull);
+            mma_finish(bars);
         }
     } else {
-        // ============ elementwise: Delta, dS, dQ epilogue (row = TMEM lane, warpgroup g = column half) ============
+        // ====== elementwise: Delta, P, dS, dQ epilogue (row = TMEM lane; warpgroup g = keys [64g, 64g+64)) ======
         const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
         const uint8_t* tDOs = smem + kOffFixed + kTileBytes;
-        uint32_t it = 0, sdp_par = 0, acc_par = 0;
+        uint32_t it = 0, s_par = 0, dp_par = 0, acc_par = 0;
         bool ok = true;
         Units u(blockIdx.x);
         uint32_t bh, qb;
@@ -387,88 +432,90 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t row = qb * kBlk + t;
             const bool valid = row < p.S_q;
             const size_t ridx = static_cast<size_t>(bh) * p.S_q + row;
-            ok = ew_all(mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrElem));
+            ok = wg_all(g, mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrElem));
             if (!ok) break;
             ++it;
-            // Delta = rowsum(dO * O): warpgroup g sums columns [64g, 64g+64) (dO from the staged
-            // tile, O from global), the halves meet in shared memory.
-            float part = 0.f, nlse2 = -INFINITY;
+            // Delta = rowsum(dO * O) of this row (dO from the staged tile, O from global); each
+            // warpgroup forms it (the two run independently); warpgroup 0 stores it.
+            float delta = 0.f, nlse2 = -INFINITY;
             if (valid) {
                 const uint4* orow = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.o) + ridx * 128);
+                float d2 = 0.f;
 #pragma unroll 4
-                for (uint32_t c = 8 * g; c < 8 * g + 8; ++c) {
+                for (uint32_t c = 0; c < 16; ++c) {
                     const uint4 a = tile_chunk(tDOs, t, c), b = __ldg(orow + c);
                     const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const float2 x = unpack2<kBF16>(aw[e]), y = unpack2<kBF16>(bw[e]);
-                        part = fmaf(x.x, y.x, fmaf(x.y, y.y, part));
+                        delta = fmaf(x.x, y.x, delta);
+                        d2 = fmaf(x.y, y.y, d2);
                     }
                 }
+                delta += d2;
                 nlse2 = -p.lse[ridx] * 1.4426950408889634f;
+                if (g == 0) p.delta[ridx] = delta;
             }
-            s_part[g * kBlk + t] = part;
-            ew_sync();
-            const float delta = s_part[t] + s_part[kBlk + t];
-            if (valid && g == 0) p.delta[ridx] = delta;
             const uint32_t nkv = kv_blocks_for(p, qb);
+            // on the diagonal block, key c of this half is visible when 64g + c <= t
+            const int32_t lim = static_cast<int32_t>(t) + 1 - static_cast<int32_t>(kHalf * g);
             for (uint32_t j = 0; j < nkv; ++j) {
-                ok = ew_all(mbar_wait_bounded(&bars->sdp_full, sdp_par, abort_flag, &g_fab_error_word, kErrElem));
-                if (!ok) break;
-                sdp_par ^= 1;
-                tc_fence_after();
-                // the diagonal block masks keys past the row (top-left causal: key k <= row)
-                const int32_t lim = static_cast<int32_t>(t) + 1 - static_cast<int32_t>(64 * g);
-                auto ds_tile = [&](auto masked) {
-#pragma unroll 1
-                    for (uint32_t c = 0; c < 2; ++c) {
-                        uint32_t s[32], dp[32], pk[16];
-                        tmem_ld32(tmem_base + 64 * g + 32 * c + lane_field, s);
-                        tmem_ld32(tmem_base + 128 + 64 * g + 32 * c + lane_field, dp);
-                        tmem_wait_ld();
+                // phase 1: S -> registers (then the MMA warp may overwrite it), P
+                if (!(ok = ew_wait(g, &bars->s_full, s_par, abort_flag))) break;
+                float pr[64];
+                {
+                    uint32_t s[64];
+                    tmem_ld32(tS + kHalf * g + lane_field, *reinterpret_cast<uint32_t(*)[32]>(s));
+                    tmem_ld32(tS + kHalf * g + 32 + lane_field, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+                    tmem_wait_ld();
+                    ew_arrive(&bars->mid);
+                    if (p.causal && j == qb) {
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            float ds[2];
+                        for (int c = 0; c < 64; ++c)
+                            pr[c] = c < lim ? ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nlse2)) : 0.f;
+                    } else {
 #pragma unroll
-                            for (int h = 0; h < 2; ++h) {
-                                float pr = ex2(fmaf(__uint_as_float(s[2 * e + h]), p.scale_log2, nlse2));
-                                if (decltype(masked)::value && static_cast<int32_t>(32 * c) + 2 * e + h >= lim) pr = 0.f;
-                                ds[h] = pr * (__uint_as_float(dp[2 * e + h]) - delta);
-                            }
-                            pk[e] = pack2<kBF16>(ds[0], ds[1]);
-                        }
-                        tmem_st16(tmem_base + 64 * g + 16 * c + lane_field, pk);
+                        for (int c = 0; c < 64; ++c) pr[c] = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nlse2));
                     }
-                };
-                if (p.causal && j == qb)
-                    ds_tile(std::true_type{});
-                else
-                    ds_tile(std::false_type{});
+                }
+                // phase 2: dS = P (dP - Delta), packed over dP
+                if (!(ok = ew_wait(g, &bars->dp_full, dp_par, abort_flag))) break;
+#pragma unroll
+                for (uint32_t c = 0; c < 2; ++c) {
+                    uint32_t dp[32], pk[16];
+                    tmem_ld32(tDP + kHalf * g + 32 * c + lane_field, dp);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        pk[e] = pack2<kBF16>(pr[32 * c + 2 * e] * (__uint_as_float(dp[2 * e]) - delta),
+                                             pr[32 * c + 2 * e + 1] * (__uint_as_float(dp[2 * e + 1]) - delta));
+                    tmem_st16(tDP + kHalf * g + 16 * c + lane_field, pk);
+                }
                 tmem_wait_st();
-                tc_fence_before();
-                mbar_arrive(&bars->ds_half[g]);
+                ew_arrive(&bars->ds_full);
             }
             if (!ok) break;
-            ok = ew_all(mbar_wait_bounded(&bars->acc_full, acc_par, abort_flag, &g_fab_error_word, kErrElem));
-            if (!ok) break;
-            acc_par ^= 1;
-            tc_fence_after();
+            if (!(ok = ew_wait(g, &bars->acc_full, acc_par, abort_flag))) break;
+            // epilogue: dQ columns [64g, 64g+64), scaled
             uint8_t* dq_row = static_cast<uint8_t*>(p.out0) + ridx * 128 * 2;
-#pragma unroll 1
-            for (uint32_t c = 0; c < 2; ++c) {
-                uint32_t acc[32], pk[16];
-                tmem_ld32(tmem_base + 256 + 64 * g + 32 * c + lane_field, acc);
-                tmem_wait_ld();
+            uint32_t acc[2][32];
+            tmem_ld32(tDQ + kHalf * g + lane_field, acc[0]);
+            tmem_ld32(tDQ + kHalf * g + 32 + lane_field, acc[1]);
+            tmem_wait_ld();
+            ew_arrive(&bars->acc_empty);
+            if (valid) {
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    pk[e] = pack2<kBF16>(__uint_as_float(acc[2 * e]) * p.scale, __uint_as_float(acc[2 * e + 1]) * p.scale);
-                if (valid) {
-                    uint4* dst = reinterpret_cast<uint4*>(dq_row + (64 * g + 32 * c) * 2);
+                for (uint32_t c = 0; c < 2; ++c) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        pk[e] = pack2<kBF16>(__uint_as_float(acc[c][2 * e]) * p.scale,
+                                             __uint_as_float(acc[c][2 * e + 1]) * p.scale);
+                    uint4* dst = reinterpret_cast<uint4*>(dq_row + (kHalf * g + 32 * c) * 2);
 #pragma unroll
                     for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
                 }
             }
-            tc_fence_before();
         }
     }
     teardown_cta(tmem_base, warp);
@@ -487,14 +534,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + sizeof(Bars));
     volatile uint32_t* abort_flag = tmem_slot + 1;
-    // per query block, double-buffered: [buf][0][128] = -lse * log2(e), [buf][1][128] = Delta
-    float* s_vec = reinterpret_cast<float*>(smem + kOffVec);
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const uint32_t nq = n_blocks(p.S_q);
     const uint32_t tmem_base = setup_cta(bars, tmem_slot, abort_flag, warp);
     const uint32_t sK = smem_u32(smem + kOffFixed), sV = sK + kTileBytes, sRing = smem_u32(smem + kOffRing);
-    // TMEM: S^T [0,128), dP^T [128,256), dV [256,384), dK [384,512); warpgroup g packs its half of
-    // P^T / dS^T into columns [64g, 64g+32) of S^T / dP^T.
+    const uint32_t tS = tmem_base, tDP = tmem_base + 128, tDV = tmem_base + 256, tDK = tmem_base + 384;
     if (warp == kTmaWarp) {
         if (lane == 0) {
             Ring ring;
@@ -527,125 +571,143 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t idesc_ss = make_idesc_f16(kBF16, 128, 128, false, false);
             const uint32_t idesc_ts = make_idesc_f16(kBF16, 128, 128, false, true);
-            const uint32_t tS = tmem_base, tDP = tmem_base + 128, tDV = tmem_base + 256, tDK = tmem_base + 384;
             RingWait ring;
-            uint32_t it = 0, ds_par = 0;
-            bool ok = true;
+            MmaPar par;
+            uint32_t it = 0;
             Units u(blockIdx.x);
             uint32_t bh, kb;
-            while (ok && u.next(p, bh, kb)) {
+            while (u.next(p, bh, kb)) {
                 const uint32_t q0 = q_first_for(p, kb);
                 if (q0 >= nq) continue;  // the producer skipped this unit too
-                if (!mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrMma)) {
-                    ok = false;
-                    break;
-                }
-                ++it;
+                if (!mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrMma)) break;
                 tc_fence_after();
-                for (uint32_t i = q0; i < nq; ++i) {
-                    uint32_t qs, os;
-                    if (!ring.next(bars, abort_flag, qs)) { ok = false; break; }
-                    issue_ss(tS, sK, sRing + qs * kTileBytes, idesc_ss);              // S^T = K Q_i^T
-                    if (!ring.next(bars, abort_flag, os)) { ok = false; break; }
-                    issue_ss(tDP, sV, sRing + os * kTileBytes, idesc_ss);             // dP^T = V dO_i^T
-                    tc_commit(&bars->sdp_full);
-                    for (uint32_t h = 0; h < 2 && ok; ++h) {                         // by query halves
-                        if (!mbar_wait_bounded(&bars->ds_half[h], ds_par, abort_flag, &g_fab_error_word, kErrMma)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const bool acc = i > q0 || h > 0;
-                        issue_ts_half(tDV, tS, sRing + os * kTileBytes, idesc_ts, h, acc);   // dV += P^T dO_i
-                        issue_ts_half(tDK, tDP, sRing + qs * kTileBytes, idesc_ts, h, acc);  // dK += dS^T Q_i
+                uint32_t qs, os;
+                if (!ring.pair(bars, abort_flag, qs, os)) break;
+                issue_ss(tS, sK, sRing + qs * kTileBytes, idesc_ss);             // S^T = K Q_q0^T
+                tc_commit(&bars->s_full);
+                issue_ss(tDP, sV, sRing + os * kTileBytes, idesc_ss);            // dP^T = V dO_q0^T
+                tc_commit(&bars->dp_full);
+                if (!mbar_wait_bounded(&bars->acc_empty, (it & 1) ^ 1, abort_flag, &g_fab_error_word, kErrMma)) break;
+                bool ok = true;
+                for (uint32_t i = q0; i < nq && ok; ++i) {
+                    const bool nxt = i + 1 < nq;
+                    uint32_t qn = 0, on = 0;
+                    // P^T_i packed over S^T: dV += P^T dO_i, then the next S^T
+                    if (!mma_wait(&bars->mid, par.mid, abort_flag)) { ok = false; break; }
+                    issue_ts(tDV, tS, sRing + os * kTileBytes, idesc_ts, i > q0);
+                    if (nxt) {
+                        if (!ring.pair(bars, abort_flag, qn, on)) { ok = false; break; }
+                        issue_ss(tS, sK, sRing + qn * kTileBytes, idesc_ss);
+                        tc_commit(&bars->s_full);
                     }
-                    if (!ok) break;
-                    ds_par ^= 1;
+                    // dS^T_i packed over dP^T: dK += dS^T Q_i, then the next dP^T
+                    if (!mma_wait(&bars->ds_full, par.ds, abort_flag)) { ok = false; break; }
+                    issue_ts(tDK, tDP, sRing + qs * kTileBytes, idesc_ts, i > q0);
+                    if (nxt) {
+                        issue_ss(tDP, sV, sRing + on * kTileBytes, idesc_ss);
+                        tc_commit(&bars->dp_full);
+                    }
                     tc_commit(&bars->ring_empty[qs]);
                     tc_commit(&bars->ring_empty[os]);
+                    qs = qn;
+                    os = on;
                 }
                 if (!ok) break;
                 tc_commit(&bars->fixed_empty);
                 tc_commit(&bars->acc_full);
+                ++it;
             }
-            tc_commit(&bars->mma_done);
-            volatile uint32_t never = 0;
-            mbar_wait_bounded(&bars->mma_done, 0, &never, &g_fab_error_word, kErrDrain, 1000000000ull);
+            mma_finish(bars);
         }
     } else {
-        // ====== elementwise: P^T, dS^T, dK/dV epilogue (key = TMEM lane, warpgroup g = query half) ======
+        // ====== elementwise: P^T, dS^T, dK/dV epilogue (key = TMEM lane; warpgroup g = queries [64g, 64g+64)) ======
         const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
-        uint32_t sdp_par = 0, acc_par = 0, nblk = 0;
+        // this warpgroup's staging, double-buffered: [buf][0..63] -lse*log2(e), [buf][64..127] Delta
+        float* vec_base = reinterpret_cast<float*>(smem + kOffVec) + g * 2 * kBlk;
+        uint32_t s_par = 0, dp_par = 0, acc_par = 0, nblk = 0;
         Units u(blockIdx.x);
         uint32_t bh, kb;
         bool ok = true;
+        // on the diagonal block, query c of this half sees the key when 64g + c >= t
+        const int32_t first = static_cast<int32_t>(t) - static_cast<int32_t>(kHalf * g);
         while (ok && u.next(p, bh, kb)) {
             const uint32_t key = kb * kBlk + t;
             const size_t kidx = static_cast<size_t>(bh) * p.S_k + key;
             const uint32_t q0 = q_first_for(p, kb);
             if (q0 < nq) {
                 for (uint32_t i = q0; i < nq; ++i, ++nblk) {
-                    // stage -lse*log2(e) (-inf past S_q, so P = 0 there) and Delta of block i.  Buffer
-                    // nblk & 1 was last read two blocks ago, before every thread passed the previous
-                    // block's barrier, which this thread has passed too.
-                    float* vec = s_vec + (nblk & 1) * 2 * kBlk;
-                    const uint32_t r = i * kBlk + t;
+                    // stage -lse*log2(e) (-inf past S_q, so P = 0 there) and Delta of this half's 64
+                    // queries.  Buffer nblk & 1 was last read two blocks ago, before every thread of
+                    // the group passed the previous block's barriers, which this thread has passed too.
+                    float* vec = vec_base + (nblk & 1) * kBlk;
+                    const uint32_t r = i * kBlk + kHalf * g + (t & 63);
                     const size_t ridx = static_cast<size_t>(bh) * p.S_q + r;
-                    if (g == 0)
+                    if (t < 64)
                         vec[t] = r < p.S_q ? -p.lse[ridx] * 1.4426950408889634f : -INFINITY;
                     else
-                        vec[kBlk + t] = r < p.S_q ? p.delta[ridx] : 0.f;
-                    // publishes the staged values and makes the give-up decision uniform
-                    ok = ew_all(mbar_wait_bounded(&bars->sdp_full, sdp_par, abort_flag, &g_fab_error_word, kErrElem));
-                    if (!ok) break;
-                    sdp_par ^= 1;
-                    tc_fence_after();
-                    // on the diagonal block, query column q sees this key when q >= t (key <= row)
-                    const int32_t first = static_cast<int32_t>(t) - static_cast<int32_t>(64 * g);
-                    auto pds_tile = [&](auto masked) {
-#pragma unroll 1
-                        for (uint32_t c = 0; c < 2; ++c) {
-                            uint32_t s[32], dp[32], pp[16], pd[16];
-                            tmem_ld32(tmem_base + 64 * g + 32 * c + lane_field, s);
-                            tmem_ld32(tmem_base + 128 + 64 * g + 32 * c + lane_field, dp);
-                            const float4* nl4 = reinterpret_cast<const float4*>(vec + 64 * g + 32 * c);
-                            const float4* dl4 = reinterpret_cast<const float4*>(vec + kBlk + 64 * g + 32 * c);
-                            tmem_wait_ld();
+                        vec[t] = r < p.S_q ? p.delta[ridx] : 0.f;
+                    // phase 1: P^T from S^T, packed over it (the wait also publishes the staged values)
+                    if (!(ok = ew_wait(g, &bars->s_full, s_par, abort_flag))) break;
+                    float pr[64];
+                    {
+                        uint32_t s[64], pk[32];
+                        tmem_ld32(tS + kHalf * g + lane_field, *reinterpret_cast<uint32_t(*)[32]>(s));
+                        tmem_ld32(tS + kHalf * g + 32 + lane_field, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+                        const float4* nl4 = reinterpret_cast<const float4*>(vec);
+                        tmem_wait_ld();
+                        if (p.causal && i == kb) {
 #pragma unroll
-                            for (int e4 = 0; e4 < 8; ++e4) {
-                                const float4 nl = nl4[e4], dl = dl4[e4];
-                                const float nla[4] = {nl.x, nl.y, nl.z, nl.w}, dla[4] = {dl.x, dl.y, dl.z, dl.w};
-                                float pr[4], ds[4];
+                            for (int e4 = 0; e4 < 16; ++e4) {
+                                const float4 nl = nl4[e4];
+                                const float nla[4] = {nl.x, nl.y, nl.z, nl.w};
 #pragma unroll
-                                for (int h = 0; h < 4; ++h) {
-                                    const int col = 4 * e4 + h;
-                                    pr[h] = ex2(fmaf(__uint_as_float(s[col]), p.scale_log2, nla[h]));
-                                    if (decltype(masked)::value && static_cast<int32_t>(32 * c) + col < first) pr[h] = 0.f;
-                                    ds[h] = pr[h] * (__uint_as_float(dp[col]) - dla[h]);
+                                for (int k = 0; k < 4; ++k) {
+                                    const int c = 4 * e4 + k;
+                                    pr[c] = c >= first ? ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nla[k])) : 0.f;
                                 }
-                                pp[2 * e4] = pack2<kBF16>(pr[0], pr[1]);
-                                pp[2 * e4 + 1] = pack2<kBF16>(pr[2], pr[3]);
-                                pd[2 * e4] = pack2<kBF16>(ds[0], ds[1]);
-                                pd[2 * e4 + 1] = pack2<kBF16>(ds[2], ds[3]);
                             }
-                            tmem_st16(tmem_base + 64 * g + 16 * c + lane_field, pp);
-                            tmem_st16(tmem_base + 128 + 64 * g + 16 * c + lane_field, pd);
+                        } else {
+#pragma unroll
+                            for (int e4 = 0; e4 < 16; ++e4) {
+                                const float4 nl = nl4[e4];
+                                const float nla[4] = {nl.x, nl.y, nl.z, nl.w};
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    pr[4 * e4 + k] = ex2(fmaf(__uint_as_float(s[4 * e4 + k]), p.scale_log2, nla[k]));
+                            }
                         }
-                    };
-                    if (p.causal && i == kb)
-                        pds_tile(std::true_type{});
-                    else
-                        pds_tile(std::false_type{});
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) pk[e] = pack2<kBF16>(pr[2 * e], pr[2 * e + 1]);
+                        tmem_st16(tS + kHalf * g + lane_field, pk);
+                        tmem_st16(tS + kHalf * g + 16 + lane_field, pk + 16);
+                        tmem_wait_st();
+                        ew_arrive(&bars->mid);
+                    }
+                    // phase 2: dS^T = P^T (dP^T - Delta), packed over dP^T
+                    if (!(ok = ew_wait(g, &bars->dp_full, dp_par, abort_flag))) break;
+#pragma unroll
+                    for (uint32_t c = 0; c < 2; ++c) {
+                        uint32_t dp[32], pk[16];
+                        tmem_ld32(tDP + kHalf * g + 32 * c + lane_field, dp);
+                        const float4* dl4 = reinterpret_cast<const float4*>(vec + 64 + 32 * c);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e4 = 0; e4 < 8; ++e4) {
+                            const float4 dl = dl4[e4];
+                            const int b = 32 * c + 4 * e4;
+                            pk[2 * e4] = pack2<kBF16>(pr[b] * (__uint_as_float(dp[4 * e4]) - dl.x),
+                                                      pr[b + 1] * (__uint_as_float(dp[4 * e4 + 1]) - dl.y));
+                            pk[2 * e4 + 1] = pack2<kBF16>(pr[b + 2] * (__uint_as_float(dp[4 * e4 + 2]) - dl.z),
+                                                          pr[b + 3] * (__uint_as_float(dp[4 * e4 + 3]) - dl.w));
+                        }
+                        tmem_st16(tDP + kHalf * g + 16 * c + lane_field, pk);
+                    }
                     tmem_wait_st();
-                    tc_fence_before();
-                    mbar_arrive(&bars->ds_half[g]);
+                    ew_arrive(&bars->ds_full);
                 }
                 if (!ok) break;
-                ok = ew_all(mbar_wait_bounded(&bars->acc_full, acc_par, abort_flag, &g_fab_error_word, kErrElem));
-                if (!ok) break;
-                acc_par ^= 1;
-                tc_fence_after();
+                if (!(ok = ew_wait(g, &bars->acc_full, acc_par, abort_flag))) break;
             }
             // epilogue: dV, dK (scaled) of this key, columns [64g, 64g+64); zeros when no query sees the block
             const bool valid = key < p.S_k;
@@ -655,9 +717,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (uint32_t c = 0; c < 2; ++c) {
                 uint32_t av[32], ak[32], pv[16], pk[16];
                 if (q0 < nq) {
-                    tmem_ld32(tmem_base + 256 + 64 * g + 32 * c + lane_field, av);
-                    tmem_ld32(tmem_base + 384 + 64 * g + 32 * c + lane_field, ak);
+                    tmem_ld32(tDV + kHalf * g + 32 * c + lane_field, av);
+                    tmem_ld32(tDK + kHalf * g + 32 * c + lane_field, ak);
                     tmem_wait_ld();
+                    if (c == 1) ew_arrive(&bars->acc_empty);  // the accumulators are read: the next unit may start them
                 } else {
 #pragma unroll
                     for (int e = 0; e < 32; ++e) av[e] = ak[e] = 0u;
@@ -668,8 +731,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     pk[e] = pack2<kBF16>(__uint_as_float(ak[2 * e]) * p.scale, __uint_as_float(ak[2 * e + 1]) * p.scale);
                 }
                 if (valid) {
-                    uint4* dv = reinterpret_cast<uint4*>(dv_row + (64 * g + 32 * c) * 2);
-                    uint4* dk = reinterpret_cast<uint4*>(dk_row + (64 * g + 32 * c) * 2);
+                    uint4* dv = reinterpret_cast<uint4*>(dv_row + (kHalf * g + 32 * c) * 2);
+                    uint4* dk = reinterpret_cast<uint4*>(dk_row + (kHalf * g + 32 * c) * 2);
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
                         dv[v] = make_uint4(pv[4 * v], pv[4 * v + 1], pv[4 * v + 2], pv[4 * v + 3]);
@@ -677,7 +740,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            tc_fence_before();
         }
     }
     teardown_cta(tmem_base, warp);
