@@ -6,7 +6,9 @@
 //
 // Tensor-core path (bf16/fp16, D = D_v = 128, 16-byte aligned buffers): two kernels with the same
 // structure.  A CTA holds two 128 x 128 "fixed" tiles of one 128-row block in shared memory and
-// streams the other side's 128-row tiles through a 4-stage TMA ring (two blocks in flight):
+// streams the other side's 128-row tiles through a 5-stage TMA ring.  Each streamed tile is released
+// as soon as its last product is issued (V_j and dO_i after one product, K_j and Q_i after two), and
+// the MMA warp waits for each tile just before its first product, so loads run about a block ahead:
 //   * fa_bwd_dq_kernel: fixed Q, dO of a query block (rows on TMEM lanes); for every visible key
 //     block j: S = Q K_j^T, dP = dO V_j^T, dS = P (dP - Delta) (16-bit), dQ += dS K_j.  It first
 //     computes Delta = rowsum(dO * O) for its rows and writes it (the caller's [B, H, S_q] fp32
@@ -61,12 +63,12 @@ constexpr uint32_t kTileBytes = 2 * kPanelBytes;  // a 128 x 128 16-bit tile: 32
 constexpr uint32_t kHalf = 64;                  // columns of a tile per elementwise warpgroup
 constexpr uint32_t kMmaWarp = 8, kTmaWarp = 9;
 constexpr uint32_t kThreads = 320;              // two elementwise warpgroups, the MMA warp, the TMA warp
-constexpr uint32_t kStages = 4;                 // streamed-tile ring: two blocks of two tiles
+constexpr uint32_t kStages = 5;                 // streamed-tile ring (tiles are released one by one)
 constexpr uint32_t kOffFixed = 0;               // two tiles resident per unit (Q,dO or K,V)
 constexpr uint32_t kOffRing = 2 * kTileBytes;
 constexpr uint32_t kOffBar = kOffRing + kStages * kTileBytes;
-constexpr uint32_t kOffVec = kOffBar + 256;     // dK/dV: per warpgroup, double-buffered -lse*log2(e) and Delta
-constexpr uint32_t kVecBytes = 2 * 2 * 2 * kHalf * 4;
+constexpr uint32_t kOffVec = kOffBar + 256;     // dK/dV: per warpgroup, -lse*log2(e) and Delta of its 64 queries
+constexpr uint32_t kVecBytes = 2 * 2 * kHalf * 4;
 constexpr uint32_t kSmemBytes = kOffVec + kVecBytes + 1024;
 
 enum : uint32_t {
@@ -205,6 +207,9 @@ __device__ __forceinline__ bool wg_all(uint32_t g, bool pred) {
     return r != 0;
 }
 
+// Plain barrier among the 128 threads of warpgroup g.
+__device__ __forceinline__ void wg_sync(uint32_t g) { asm volatile("bar.sync %0, 128;" ::"r"(2 + g) : "memory"); }
+
 // Shared setup of both kernels: barriers, TMEM (512 columns, MMA warp), and the bounded-wait state.
 __device__ __forceinline__ uint32_t setup_cta(Bars* bars, uint32_t* tmem_slot, volatile uint32_t* abort_flag,
                                               uint32_t warp) {
@@ -277,22 +282,18 @@ struct Ring {
     }
 };
 
-// The MMA warp's consumer side of the ring: the next block's two streamed tiles.
+// The MMA warp's consumer side of the ring, in the producer's order.
 struct RingWait {
     uint32_t stage = 0, phase = 0;
     __device__ __forceinline__ bool one(Bars* bars, volatile uint32_t* abort_flag, uint32_t& st) {
         if (!mbar_wait_bounded(&bars->ring_full[stage], phase, abort_flag, &g_fab_error_word, kErrMma)) return false;
+        tc_fence_after();
         st = stage;
         if (++stage == kStages) {
             stage = 0;
             phase ^= 1;
         }
         return true;
-    }
-    __device__ __forceinline__ bool pair(Bars* bars, volatile uint32_t* abort_flag, uint32_t& x, uint32_t& y) {
-        const bool ok = one(bars, abort_flag, x) && one(bars, abort_flag, y);
-        tc_fence_after();
-        return ok;
     }
 };
 
@@ -384,11 +385,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrMma)) break;
                 tc_fence_after();
                 uint32_t ks, vs;
-                if (!ring.pair(bars, abort_flag, ks, vs)) break;
+                if (!ring.one(bars, abort_flag, ks)) break;
                 issue_ss(tS, sQ, sRing + ks * kTileBytes, idesc_ss);             // S_0 = Q K_0^T
                 tc_commit(&bars->s_full);
+                if (!ring.one(bars, abort_flag, vs)) break;
                 issue_ss(tDP, sDO, sRing + vs * kTileBytes, idesc_ss);           // dP_0 = dO V_0^T
                 tc_commit(&bars->dp_full);
+                tc_commit(&bars->ring_empty[vs]);                                // V_0 has no other reader
                 if (!mbar_wait_bounded(&bars->acc_empty, (it & 1) ^ 1, abort_flag, &g_fab_error_word, kErrMma)) break;
                 bool ok = true;
                 for (uint32_t j = 0; j < n && ok; ++j) {
@@ -397,21 +400,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // S_j has been read into registers: the next S goes into its columns
                     if (!mma_wait(&bars->mid, par.mid, abort_flag)) { ok = false; break; }
                     if (nxt) {
-                        if (!ring.pair(bars, abort_flag, kn, vn)) { ok = false; break; }
+                        if (!ring.one(bars, abort_flag, kn)) { ok = false; break; }
                         issue_ss(tS, sQ, sRing + kn * kTileBytes, idesc_ss);
                         tc_commit(&bars->s_full);
                     }
                     // dS_j packed over dP_j: dQ += dS_j K_j, then the next dP into those columns
                     if (!mma_wait(&bars->ds_full, par.ds, abort_flag)) { ok = false; break; }
                     issue_ts(tDQ, tDP, sRing + ks * kTileBytes, idesc_ts, j > 0);
+                    tc_commit(&bars->ring_empty[ks]);
                     if (nxt) {
+                        if (!ring.one(bars, abort_flag, vn)) { ok = false; break; }
                         issue_ss(tDP, sDO, sRing + vn * kTileBytes, idesc_ss);
                         tc_commit(&bars->dp_full);
+                        tc_commit(&bars->ring_empty[vn]);
                     }
-                    tc_commit(&bars->ring_empty[ks]);
-                    tc_commit(&bars->ring_empty[vs]);
                     ks = kn;
-                    vs = vn;
                 }
                 if (!ok) break;
                 tc_commit(&bars->fixed_empty);
@@ -582,9 +585,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrMma)) break;
                 tc_fence_after();
                 uint32_t qs, os;
-                if (!ring.pair(bars, abort_flag, qs, os)) break;
+                if (!ring.one(bars, abort_flag, qs)) break;
                 issue_ss(tS, sK, sRing + qs * kTileBytes, idesc_ss);             // S^T = K Q_q0^T
                 tc_commit(&bars->s_full);
+                if (!ring.one(bars, abort_flag, os)) break;
                 issue_ss(tDP, sV, sRing + os * kTileBytes, idesc_ss);            // dP^T = V dO_q0^T
                 tc_commit(&bars->dp_full);
                 if (!mbar_wait_bounded(&bars->acc_empty, (it & 1) ^ 1, abort_flag, &g_fab_error_word, kErrMma)) break;
@@ -595,20 +599,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // P^T_i packed over S^T: dV += P^T dO_i, then the next S^T
                     if (!mma_wait(&bars->mid, par.mid, abort_flag)) { ok = false; break; }
                     issue_ts(tDV, tS, sRing + os * kTileBytes, idesc_ts, i > q0);
+                    tc_commit(&bars->ring_empty[os]);                            // dO_i is done
                     if (nxt) {
-                        if (!ring.pair(bars, abort_flag, qn, on)) { ok = false; break; }
+                        if (!ring.one(bars, abort_flag, qn)) { ok = false; break; }
                         issue_ss(tS, sK, sRing + qn * kTileBytes, idesc_ss);
                         tc_commit(&bars->s_full);
                     }
                     // dS^T_i packed over dP^T: dK += dS^T Q_i, then the next dP^T
                     if (!mma_wait(&bars->ds_full, par.ds, abort_flag)) { ok = false; break; }
                     issue_ts(tDK, tDP, sRing + qs * kTileBytes, idesc_ts, i > q0);
+                    tc_commit(&bars->ring_empty[qs]);                            // Q_i is done
                     if (nxt) {
+                        if (!ring.one(bars, abort_flag, on)) { ok = false; break; }
                         issue_ss(tDP, sV, sRing + on * kTileBytes, idesc_ss);
                         tc_commit(&bars->dp_full);
                     }
-                    tc_commit(&bars->ring_empty[qs]);
-                    tc_commit(&bars->ring_empty[os]);
                     qs = qn;
                     os = on;
                 }
@@ -623,9 +628,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ====== elementwise: P^T, dS^T, dK/dV epilogue (key = TMEM lane; warpgroup g = queries [64g, 64g+64)) ======
         const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
-        // this warpgroup's staging, double-buffered: [buf][0..63] -lse*log2(e), [buf][64..127] Delta
-        float* vec_base = reinterpret_cast<float*>(smem + kOffVec) + g * 2 * kBlk;
-        uint32_t s_par = 0, dp_par = 0, acc_par = 0, nblk = 0;
+        // this warpgroup's staging: [0..63] -lse*log2(e), [64..127] Delta
+        float* vec = reinterpret_cast<float*>(smem + kOffVec) + g * kBlk;
+        uint32_t s_par = 0, dp_par = 0, acc_par = 0;
         Units u(blockIdx.x);
         uint32_t bh, kb;
         bool ok = true;
@@ -636,13 +641,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const size_t kidx = static_cast<size_t>(bh) * p.S_k + key;
             const uint32_t q0 = q_first_for(p, kb);
             if (q0 < nq) {
-                for (uint32_t i = q0; i < nq; ++i, ++nblk) {
+                for (uint32_t i = q0; i < nq; ++i) {
                     // stage -lse*log2(e) (-inf past S_q, so P = 0 there) and Delta of this half's 64
-                    // queries.  Buffer nblk & 1 was last read two blocks ago, before every thread of
-                    // the group passed the previous block's barriers, which this thread has passed too.
-                    float* vec = vec_base + (nblk & 1) * kBlk;
+                    // queries, once every thread of the group is done with the previous block's
                     const uint32_t r = i * kBlk + kHalf * g + (t & 63);
                     const size_t ridx = static_cast<size_t>(bh) * p.S_q + r;
+                    wg_sync(g);
                     if (t < 64)
                         vec[t] = r < p.S_q ? -p.lse[ridx] * 1.4426950408889634f : -INFINITY;
                     else
