@@ -12,7 +12,8 @@
 //   * fa_bwd_dq_kernel: fixed Q, dO of a query block (rows on TMEM lanes); for every visible key
 //     block j: S = Q K_j^T, dP = dO V_j^T, dS = P (dP - Delta) (16-bit), dQ += dS K_j.  It first
 //     computes Delta = rowsum(dO * O) for its rows and writes it (the caller's [B, H, S_q] fp32
-//     buffer).  TMEM: S [0,128), dP [128,256) (dS packed over it), dQ [256,384).
+//     buffer).  TMEM: S [0,128), dP in two buffers [128,256) and [256,384) (block j in buffer j & 1,
+//     dS packed over it), dQ [384,512).
 //   * fa_bwd_dkdv_kernel (launched after, it reads Delta): fixed K, V of a key block (keys on
 //     TMEM lanes); for every query block i that sees the keys: S^T = K Q_i^T, dP^T = V dO_i^T,
 //     P^T (16-bit, over S^T), dS^T (16-bit, over dP^T), dV += P^T dO_i, dK += dS^T Q_i.
@@ -22,9 +23,9 @@
 // elementwise warpgroups (warps 0-3 and 4-7; a thread owns one TMEM lane, warpgroup g the 64 columns
 // [64g, 64g+64) of each tile) work in two phases per block, each with its own hand-off to the MMA
 // warp (warp 8), which keeps the tensor pipe busy during both:
-//   dQ:    phase 1 loads S and releases it (s_free; the next S is issued at once), forms P in
-//          registers; phase 2 forms dS from dP and packs it over dP (ds_full): dQ += dS K_j, then
-//          the next dP.
+//   dQ:    phase 1 loads S and releases it (the next S is issued at once), forms P in registers;
+//          phase 2 forms dS from dP and packs it over dP (ds_full): dQ += dS K_j, then dP of block
+//          j + 2 into the same buffer, so phase 2 of the next block never waits for this product.
 //   dK/dV: phase 1 forms P^T from S^T and packs it over S^T (p_full): dV += P^T dO_i, then the next
 //          S^T; phase 2 forms dS^T and packs it over dP^T (ds_full): dK += dS^T Q_i, then the next
 //          dP^T.
@@ -93,7 +94,7 @@ struct Params {
 struct Bars {
     uint64_t fixed_full, fixed_empty;
     uint64_t ring_full[kStages], ring_empty[kStages];
-    uint64_t s_full, dp_full;      // MMA -> elementwise: S (S^T) and dP (dP^T) of the block are in TMEM
+    uint64_t s_full, dp_full[2];   // MMA -> elementwise: S (S^T) and dP (dP^T, buffer b) of the block are in TMEM
     uint64_t mid, ds_full;         // elementwise -> MMA (256 arrivals): phase 1 done (dQ: S read; dK/dV: P^T packed), phase 2 (dS packed)
     uint64_t acc_full, acc_empty;
     uint64_t mma_done;
@@ -221,7 +222,8 @@ __device__ __forceinline__ uint32_t setup_cta(Bars* bars, uint32_t* tmem_slot, v
             mbar_init(&bars->ring_empty[s], 1);
         }
         mbar_init(&bars->s_full, 1);
-        mbar_init(&bars->dp_full, 1);
+        mbar_init(&bars->dp_full[0], 1);
+        mbar_init(&bars->dp_full[1], 1);
         mbar_init(&bars->mid, 256);
         mbar_init(&bars->ds_full, 256);
         mbar_init(&bars->acc_full, 1);
@@ -315,6 +317,84 @@ __device__ __forceinline__ void mma_finish(Bars* bars) {
     mbar_wait_bounded(&bars->mma_done, 0, &never, &g_fab_error_word, kErrDrain, 1000000000ull);
 }
 
+// The MMA warp runs converged: every lane computes the same descriptors and waits on the same
+// barriers (their give-up decisions ANDed over the warp), and only the elected lane issues the
+// tcgen05.mma / tcgen05.commit instructions, predicated.  Warp-uniform descriptor values keep the
+// issuing lane's stream between two MMAs short.
+struct Issuer {
+    uint32_t leader;
+    __device__ __forceinline__ bool wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag) const {
+        const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, abort_flag, &g_fab_error_word, kErrMma));
+        if (ok) tc_fence_after();
+        return ok;
+    }
+    __device__ __forceinline__ bool wait_flip(uint64_t* bar, uint32_t& par, volatile uint32_t* abort_flag) const {
+        if (!wait(bar, par, abort_flag)) return false;
+        par ^= 1;
+        return true;
+    }
+    __device__ __forceinline__ void commit(uint64_t* bar) const {
+        asm volatile(
+            "{\n\t.reg .pred q;\n\t"
+            "setp.ne.b32 q, %1, 0;\n\t"
+            "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar)),
+            "r"(leader)
+            : "memory");
+    }
+    __device__ __forceinline__ void mma_ss(uint32_t d, Sw128Desc a, Sw128Desc b, uint32_t idesc, uint32_t acc) const {
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\t.reg .b64 da, db;\n\t"
+            "setp.ne.b32 q, %7, 0;\n\t"
+            "mov.b64 da, {%1, %2};\n\tmov.b64 db, {%3, %4};\n\t"
+            "setp.ne.b32 p, %6, 0;\n\t"
+            "@q tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d),
+            "r"(a.lo), "r"(a.hi), "r"(b.lo), "r"(b.hi), "r"(idesc), "r"(acc), "r"(leader)
+            : "memory");
+    }
+    __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, Sw128Desc b, uint32_t idesc, uint32_t acc) const {
+        asm volatile(
+            "{\n\t.reg .pred p, q;\n\t.reg .b64 db;\n\t"
+            "setp.ne.b32 q, %6, 0;\n\t"
+            "mov.b64 db, {%2, %3};\n\t"
+            "setp.ne.b32 p, %5, 0;\n\t"
+            "@q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d),
+            "r"(a_tmem), "r"(b.lo), "r"(b.hi), "r"(idesc), "r"(acc), "r"(leader)
+            : "memory");
+    }
+    // the products of issue_ss / issue_ts
+    __device__ __forceinline__ void ss(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr, uint32_t idesc) const {
+        const Sw128Desc ad = make_sw128_desc2(a_addr, 16, 1024), bd = make_sw128_desc2(b_addr, 16, 1024);
+#pragma unroll
+        for (uint32_t kk = 0; kk < 8; ++kk) {
+            const uint32_t off = ((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4;
+            mma_ss(d_tmem, Sw128Desc{ad.lo + off, ad.hi}, Sw128Desc{bd.lo + off, bd.hi}, idesc, kk > 0);
+        }
+    }
+    __device__ __forceinline__ void ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, uint32_t idesc,
+                                       bool accumulate) const {
+        const Sw128Desc bd = make_sw128_desc2(b_addr, kPanelBytes, 1024);
+#pragma unroll
+        for (uint32_t kk = 0; kk < 8; ++kk)
+            mma_ts(d_tmem, a_tmem + (kk >> 2) * kHalf + (kk & 3) * 8, Sw128Desc{bd.lo + kk * (2048 >> 4), bd.hi}, idesc,
+                   (accumulate || kk > 0) ? 1u : 0u);
+    }
+    __device__ __forceinline__ bool ring_one(RingWait& ring, Bars* bars, volatile uint32_t* abort_flag,
+                                             uint32_t& st) const {
+        if (!wait(&bars->ring_full[ring.stage], ring.phase, abort_flag)) return false;
+        st = ring.stage;
+        if (++ring.stage == kStages) {
+            ring.stage = 0;
+            ring.phase ^= 1;
+        }
+        return true;
+    }
+    __device__ __forceinline__ void finish(Bars* bars) const {
+        commit(&bars->mma_done);
+        volatile uint32_t never = 0;
+        mbar_wait_bounded(&bars->mma_done, 0, &never, &g_fab_error_word, kErrDrain, 1000000000ull);
+    }
+};
+
 // Elementwise side: waits on an MMA barrier, decided for the whole warpgroup.
 __device__ __forceinline__ bool ew_wait(uint32_t g, uint64_t* bar, uint32_t& par, volatile uint32_t* abort_flag) {
     if (!wg_all(g, mbar_wait_bounded(bar, par, abort_flag, &g_fab_error_word, kErrElem))) return false;
@@ -344,7 +424,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const uint32_t tmem_base = setup_cta(bars, tmem_slot, abort_flag, warp);
     const uint32_t sQ = smem_u32(smem + kOffFixed), sDO = sQ + kTileBytes, sRing = smem_u32(smem + kOffRing);
-    const uint32_t tS = tmem_base, tDP = tmem_base + 128, tDQ = tmem_base + 256;
+    const uint32_t tS = tmem_base, tDQ = tmem_base + 384;
+    auto tDP = [&](uint32_t b) { return tmem_base + 128 + 128 * b; };
     if (warp == kTmaWarp) {
         if (lane == 0) {
             Ring ring;
@@ -366,13 +447,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 fixed_pending = static_cast<int32_t>(it & 1);
                 const uint32_t nkv = kv_blocks_for(p, qb);
-                for (uint32_t j = 0; j < nkv && ok; ++j)  // K_j, then V_j
-                    ok = ring.load(bars, smem, &tm_k, j, bh, abort_flag) && ring.load(bars, smem, &tm_v, j, bh, abort_flag);
+                // the MMA warp's order: K_0, V_0, then V_m ahead of K_m (dP runs a block ahead of S)
+                ok = ring.load(bars, smem, &tm_k, 0, bh, abort_flag) && ring.load(bars, smem, &tm_v, 0, bh, abort_flag);
+                for (uint32_t m = 1; m < nkv && ok; ++m)
+                    ok = ring.load(bars, smem, &tm_v, m, bh, abort_flag) && ring.load(bars, smem, &tm_k, m, bh, abort_flag);
             }
             if (!ok) ring.drain(bars, fixed_pending);
         }
     } else if (warp == kMmaWarp) {
-        if (lane == 0) {
+        {
+            const Issuer is{elect_one() ? 1u : 0u};
             const uint32_t idesc_ss = make_idesc_f16(kBF16, 128, 128, false, false);
             const uint32_t idesc_ts = make_idesc_f16(kBF16, 128, 128, false, true);
             RingWait ring;
@@ -382,52 +466,55 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t bh, qb;
             for (; u.next(p, bh, qb); ++it) {
                 const uint32_t n = kv_blocks_for(p, qb);
-                if (!mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrMma)) break;
+                if (!is.wait(&bars->fixed_full, it & 1, abort_flag)) break;
                 tc_fence_after();
                 uint32_t ks, vs;
-                if (!ring.one(bars, abort_flag, ks)) break;
-                issue_ss(tS, sQ, sRing + ks * kTileBytes, idesc_ss);             // S_0 = Q K_0^T
-                tc_commit(&bars->s_full);
-                if (!ring.one(bars, abort_flag, vs)) break;
-                issue_ss(tDP, sDO, sRing + vs * kTileBytes, idesc_ss);           // dP_0 = dO V_0^T
-                tc_commit(&bars->dp_full);
-                tc_commit(&bars->ring_empty[vs]);                                // V_0 has no other reader
-                if (!mbar_wait_bounded(&bars->acc_empty, (it & 1) ^ 1, abort_flag, &g_fab_error_word, kErrMma)) break;
+                if (!is.ring_one(ring, bars, abort_flag, ks)) break;
+                is.ss(tS, sQ, sRing + ks * kTileBytes, idesc_ss);             // S_0 = Q K_0^T
+                is.commit(&bars->s_full);
                 bool ok = true;
+                for (uint32_t b = 0; b < 2 && b < n && ok; ++b) {                // dP_0, dP_1 = dO V_b^T
+                    if (!is.ring_one(ring, bars, abort_flag, vs)) { ok = false; break; }
+                    is.ss(tDP(b), sDO, sRing + vs * kTileBytes, idesc_ss);
+                    is.commit(&bars->dp_full[b]);
+                    is.commit(&bars->ring_empty[vs]);                            // V has no other reader
+                }
+                if (!ok) break;
+                if (!is.wait(&bars->acc_empty, (it & 1) ^ 1, abort_flag)) break;
                 for (uint32_t j = 0; j < n && ok; ++j) {
                     const bool nxt = j + 1 < n;
                     uint32_t kn = 0, vn = 0;
                     // S_j has been read into registers: the next S goes into its columns
-                    if (!mma_wait(&bars->mid, par.mid, abort_flag)) { ok = false; break; }
+                    if (!is.wait_flip(&bars->mid, par.mid, abort_flag)) { ok = false; break; }
                     if (nxt) {
-                        if (!ring.one(bars, abort_flag, kn)) { ok = false; break; }
-                        issue_ss(tS, sQ, sRing + kn * kTileBytes, idesc_ss);
-                        tc_commit(&bars->s_full);
+                        if (!is.ring_one(ring, bars, abort_flag, kn)) { ok = false; break; }
+                        is.ss(tS, sQ, sRing + kn * kTileBytes, idesc_ss);
+                        is.commit(&bars->s_full);
                     }
-                    // dS_j packed over dP_j: dQ += dS_j K_j, then the next dP into those columns
-                    if (!mma_wait(&bars->ds_full, par.ds, abort_flag)) { ok = false; break; }
-                    issue_ts(tDQ, tDP, sRing + ks * kTileBytes, idesc_ts, j > 0);
-                    tc_commit(&bars->ring_empty[ks]);
-                    if (nxt) {
-                        if (!ring.one(bars, abort_flag, vn)) { ok = false; break; }
-                        issue_ss(tDP, sDO, sRing + vn * kTileBytes, idesc_ss);
-                        tc_commit(&bars->dp_full);
-                        tc_commit(&bars->ring_empty[vn]);
+                    // dS_j packed over dP_j: dQ += dS_j K_j, then dP_{j+2} into that buffer
+                    if (!is.wait_flip(&bars->ds_full, par.ds, abort_flag)) { ok = false; break; }
+                    is.ts(tDQ, tDP(j & 1), sRing + ks * kTileBytes, idesc_ts, j > 0);
+                    is.commit(&bars->ring_empty[ks]);
+                    if (j + 2 < n) {
+                        if (!is.ring_one(ring, bars, abort_flag, vn)) { ok = false; break; }
+                        is.ss(tDP(j & 1), sDO, sRing + vn * kTileBytes, idesc_ss);
+                        is.commit(&bars->dp_full[j & 1]);
+                        is.commit(&bars->ring_empty[vn]);
                     }
                     ks = kn;
                 }
                 if (!ok) break;
-                tc_commit(&bars->fixed_empty);
-                tc_commit(&bars->acc_full);
+                is.commit(&bars->fixed_empty);
+                is.commit(&bars->acc_full);
             }
-            mma_finish(bars);
+            is.finish(bars);
         }
     } else {
         // ====== elementwise: Delta, P, dS, dQ epilogue (row = TMEM lane; warpgroup g = keys [64g, 64g+64)) ======
         const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
         const uint8_t* tDOs = smem + kOffFixed + kTileBytes;
-        uint32_t it = 0, s_par = 0, dp_par = 0, acc_par = 0;
+        uint32_t it = 0, s_par = 0, dp_par[2] = {0, 0}, acc_par = 0;
         bool ok = true;
         Units u(blockIdx.x);
         uint32_t bh, qb;
@@ -482,17 +569,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 // phase 2: dS = P (dP - Delta), packed over dP
-                if (!(ok = ew_wait(g, &bars->dp_full, dp_par, abort_flag))) break;
+                const uint32_t buf = j & 1;
+                if (!(ok = ew_wait(g, &bars->dp_full[buf], dp_par[buf], abort_flag))) break;
 #pragma unroll
                 for (uint32_t c = 0; c < 2; ++c) {
                     uint32_t dp[32], pk[16];
-                    tmem_ld32(tDP + kHalf * g + 32 * c + lane_field, dp);
+                    tmem_ld32(tDP(buf) + kHalf * g + 32 * c + lane_field, dp);
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
                         pk[e] = pack2<kBF16>(pr[32 * c + 2 * e] * (__uint_as_float(dp[2 * e]) - delta),
                                              pr[32 * c + 2 * e + 1] * (__uint_as_float(dp[2 * e + 1]) - delta));
-                    tmem_st16(tDP + kHalf * g + 16 * c + lane_field, pk);
+                    tmem_st16(tDP(buf) + kHalf * g + 16 * c + lane_field, pk);
                 }
                 tmem_wait_st();
                 ew_arrive(&bars->ds_full);
@@ -571,7 +659,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) ring.drain(bars, fixed_pending);
         }
     } else if (warp == kMmaWarp) {
-        if (lane == 0) {
+        {
+            const Issuer is{elect_one() ? 1u : 0u};
             const uint32_t idesc_ss = make_idesc_f16(kBF16, 128, 128, false, false);
             const uint32_t idesc_ts = make_idesc_f16(kBF16, 128, 128, false, true);
             RingWait ring;
@@ -582,47 +671,47 @@ __global__ void __launch_bounds__(kThreads, 1)
             while (u.next(p, bh, kb)) {
                 const uint32_t q0 = q_first_for(p, kb);
                 if (q0 >= nq) continue;  // the producer skipped this unit too
-                if (!mbar_wait_bounded(&bars->fixed_full, it & 1, abort_flag, &g_fab_error_word, kErrMma)) break;
+                if (!is.wait(&bars->fixed_full, it & 1, abort_flag)) break;
                 tc_fence_after();
                 uint32_t qs, os;
-                if (!ring.one(bars, abort_flag, qs)) break;
-                issue_ss(tS, sK, sRing + qs * kTileBytes, idesc_ss);             // S^T = K Q_q0^T
-                tc_commit(&bars->s_full);
-                if (!ring.one(bars, abort_flag, os)) break;
-                issue_ss(tDP, sV, sRing + os * kTileBytes, idesc_ss);            // dP^T = V dO_q0^T
-                tc_commit(&bars->dp_full);
-                if (!mbar_wait_bounded(&bars->acc_empty, (it & 1) ^ 1, abort_flag, &g_fab_error_word, kErrMma)) break;
+                if (!is.ring_one(ring, bars, abort_flag, qs)) break;
+                is.ss(tS, sK, sRing + qs * kTileBytes, idesc_ss);             // S^T = K Q_q0^T
+                is.commit(&bars->s_full);
+                if (!is.ring_one(ring, bars, abort_flag, os)) break;
+                is.ss(tDP, sV, sRing + os * kTileBytes, idesc_ss);            // dP^T = V dO_q0^T
+                is.commit(&bars->dp_full[0]);
+                if (!is.wait(&bars->acc_empty, (it & 1) ^ 1, abort_flag)) break;
                 bool ok = true;
                 for (uint32_t i = q0; i < nq && ok; ++i) {
                     const bool nxt = i + 1 < nq;
                     uint32_t qn = 0, on = 0;
                     // P^T_i packed over S^T: dV += P^T dO_i, then the next S^T
-                    if (!mma_wait(&bars->mid, par.mid, abort_flag)) { ok = false; break; }
-                    issue_ts(tDV, tS, sRing + os * kTileBytes, idesc_ts, i > q0);
-                    tc_commit(&bars->ring_empty[os]);                            // dO_i is done
+                    if (!is.wait_flip(&bars->mid, par.mid, abort_flag)) { ok = false; break; }
+                    is.ts(tDV, tS, sRing + os * kTileBytes, idesc_ts, i > q0);
+                    is.commit(&bars->ring_empty[os]);                            // dO_i is done
                     if (nxt) {
-                        if (!ring.one(bars, abort_flag, qn)) { ok = false; break; }
-                        issue_ss(tS, sK, sRing + qn * kTileBytes, idesc_ss);
-                        tc_commit(&bars->s_full);
+                        if (!is.ring_one(ring, bars, abort_flag, qn)) { ok = false; break; }
+                        is.ss(tS, sK, sRing + qn * kTileBytes, idesc_ss);
+                        is.commit(&bars->s_full);
                     }
                     // dS^T_i packed over dP^T: dK += dS^T Q_i, then the next dP^T
-                    if (!mma_wait(&bars->ds_full, par.ds, abort_flag)) { ok = false; break; }
-                    issue_ts(tDK, tDP, sRing + qs * kTileBytes, idesc_ts, i > q0);
-                    tc_commit(&bars->ring_empty[qs]);                            // Q_i is done
+                    if (!is.wait_flip(&bars->ds_full, par.ds, abort_flag)) { ok = false; break; }
+                    is.ts(tDK, tDP, sRing + qs * kTileBytes, idesc_ts, i > q0);
+                    is.commit(&bars->ring_empty[qs]);                            // Q_i is done
                     if (nxt) {
-                        if (!ring.one(bars, abort_flag, on)) { ok = false; break; }
-                        issue_ss(tDP, sV, sRing + on * kTileBytes, idesc_ss);
-                        tc_commit(&bars->dp_full);
+                        if (!is.ring_one(ring, bars, abort_flag, on)) { ok = false; break; }
+                        is.ss(tDP, sV, sRing + on * kTileBytes, idesc_ss);
+                        is.commit(&bars->dp_full[0]);
                     }
                     qs = qn;
                     os = on;
                 }
                 if (!ok) break;
-                tc_commit(&bars->fixed_empty);
-                tc_commit(&bars->acc_full);
+                is.commit(&bars->fixed_empty);
+                is.commit(&bars->acc_full);
                 ++it;
             }
-            mma_finish(bars);
+            is.finish(bars);
         }
     } else {
         // ====== elementwise: P^T, dS^T, dK/dV epilogue (key = TMEM lane; warpgroup g = queries [64g, 64g+64)) ======
@@ -689,7 +778,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ew_arrive(&bars->mid);
                     }
                     // phase 2: dS^T = P^T (dP^T - Delta), packed over dP^T
-                    if (!(ok = ew_wait(g, &bars->dp_full, dp_par, abort_flag))) break;
+                    if (!(ok = ew_wait(g, &bars->dp_full[0], dp_par, abort_flag))) break;
 #pragma unroll
                     for (uint32_t c = 0; c < 2; ++c) {
                         uint32_t dp[32], pk[16];
