@@ -61,15 +61,19 @@ using namespace sm100;
 constexpr uint32_t kBlk = 128;                  // rows (queries or keys) per block
 constexpr uint32_t kPanelBytes = 128 * 64 * 2;  // one 64-column swizzle panel of a 128-row tile: 16 KB
 constexpr uint32_t kTileBytes = 2 * kPanelBytes;  // a 128 x 128 16-bit tile: 32 KB
-constexpr uint32_t kHalf = 64;                  // columns of a tile per elementwise warpgroup
-constexpr uint32_t kMmaWarp = 8, kTmaWarp = 9;
-constexpr uint32_t kThreads = 320;              // two elementwise warpgroups, the MMA warp, the TMA warp
+constexpr uint32_t kWG = 2;                     // elementwise warpgroups
+constexpr uint32_t kCols = kBlk / kWG;          // columns of a tile per warpgroup
+constexpr uint32_t kChunks = kCols / 32;        // 32-column TMEM loads per thread and tile
+constexpr uint32_t kStepsWG = kCols / 16;       // K-steps of a TMEM-operand product per warpgroup
+constexpr uint32_t kElem = 128 * kWG;           // elementwise threads
+constexpr uint32_t kMmaWarp = 4 * kWG, kTmaWarp = 4 * kWG + 1;
+constexpr uint32_t kThreads = kElem + 64;       // elementwise warpgroups, the MMA warp, the TMA warp
 constexpr uint32_t kStages = 5;                 // streamed-tile ring (tiles are released one by one)
 constexpr uint32_t kOffFixed = 0;               // two tiles resident per unit (Q,dO or K,V)
 constexpr uint32_t kOffRing = 2 * kTileBytes;
 constexpr uint32_t kOffBar = kOffRing + kStages * kTileBytes;
 constexpr uint32_t kOffVec = kOffBar + 256;     // dK/dV: per warpgroup, -lse*log2(e) and Delta of its 64 queries
-constexpr uint32_t kVecBytes = 2 * 2 * kHalf * 4;
+constexpr uint32_t kVecBytes = kWG * 2 * kCols * 4;
 constexpr uint32_t kSmemBytes = kOffVec + kVecBytes + 1024;
 
 enum : uint32_t {
@@ -166,7 +170,7 @@ __device__ __forceinline__ void issue_ts(uint32_t d_tmem, uint32_t a_tmem, uint3
     const Sw128Desc bd = make_sw128_desc2(b_addr, kPanelBytes, 1024);
 #pragma unroll
     for (uint32_t kk = 0; kk < 8; ++kk)
-        mma_ts2(d_tmem, a_tmem + (kk >> 2) * kHalf + (kk & 3) * 8, Sw128Desc{bd.lo + kk * (2048 >> 4), bd.hi}, idesc,
+        mma_ts2(d_tmem, a_tmem + (kk / kStepsWG) * kCols + (kk % kStepsWG) * 8, Sw128Desc{bd.lo + kk * (2048 >> 4), bd.hi}, idesc,
                 (accumulate || kk > 0) ? 1u : 0u);
 }
 
@@ -224,10 +228,10 @@ __device__ __forceinline__ uint32_t setup_cta(Bars* bars, uint32_t* tmem_slot, v
         mbar_init(&bars->s_full, 1);
         mbar_init(&bars->dp_full[0], 1);
         mbar_init(&bars->dp_full[1], 1);
-        mbar_init(&bars->mid, 256);
-        mbar_init(&bars->ds_full, 256);
+        mbar_init(&bars->mid, kElem);
+        mbar_init(&bars->ds_full, kElem);
         mbar_init(&bars->acc_full, 1);
-        mbar_init(&bars->acc_empty, 256);
+        mbar_init(&bars->acc_empty, kElem);
         mbar_init(&bars->mma_done, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -375,7 +379,7 @@ struct Issuer {
         const Sw128Desc bd = make_sw128_desc2(b_addr, kPanelBytes, 1024);
 #pragma unroll
         for (uint32_t kk = 0; kk < 8; ++kk)
-            mma_ts(d_tmem, a_tmem + (kk >> 2) * kHalf + (kk & 3) * 8, Sw128Desc{bd.lo + kk * (2048 >> 4), bd.hi}, idesc,
+            mma_ts(d_tmem, a_tmem + (kk / kStepsWG) * kCols + (kk % kStepsWG) * 8, Sw128Desc{bd.lo + kk * (2048 >> 4), bd.hi}, idesc,
                    (accumulate || kk > 0) ? 1u : 0u);
     }
     __device__ __forceinline__ bool ring_one(RingWait& ring, Bars* bars, volatile uint32_t* abort_flag,
@@ -547,62 +551,64 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (g == 0) p.delta[ridx] = delta;
             }
             const uint32_t nkv = kv_blocks_for(p, qb);
-            // on the diagonal block, key c of this half is visible when 64g + c <= t
-            const int32_t lim = static_cast<int32_t>(t) + 1 - static_cast<int32_t>(kHalf * g);
+            // on the diagonal block, key c of this warpgroup's columns is visible when kCols*g + c <= t
+            const int32_t lim = static_cast<int32_t>(t) + 1 - static_cast<int32_t>(kCols * g);
             for (uint32_t j = 0; j < nkv; ++j) {
                 // phase 1: S -> registers (then the MMA warp may overwrite it), P
                 if (!(ok = ew_wait(g, &bars->s_full, s_par, abort_flag))) break;
-                float pr[64];
+                float pr[kCols];
                 {
-                    uint32_t s[64];
-                    tmem_ld32(tS + kHalf * g + lane_field, *reinterpret_cast<uint32_t(*)[32]>(s));
-                    tmem_ld32(tS + kHalf * g + 32 + lane_field, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+                    uint32_t s[kCols];
+#pragma unroll
+                    for (uint32_t c = 0; c < kChunks; ++c)
+                        tmem_ld32(tS + kCols * g + 32 * c + lane_field, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c));
                     tmem_wait_ld();
                     ew_arrive(&bars->mid);
                     if (p.causal && j == qb) {
 #pragma unroll
-                        for (int c = 0; c < 64; ++c)
+                        for (int c = 0; c < static_cast<int>(kCols); ++c)
                             pr[c] = c < lim ? ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nlse2)) : 0.f;
                     } else {
 #pragma unroll
-                        for (int c = 0; c < 64; ++c) pr[c] = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nlse2));
+                        for (int c = 0; c < static_cast<int>(kCols); ++c)
+                            pr[c] = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, nlse2));
                     }
                 }
                 // phase 2: dS = P (dP - Delta), packed over dP
                 const uint32_t buf = j & 1;
                 if (!(ok = ew_wait(g, &bars->dp_full[buf], dp_par[buf], abort_flag))) break;
 #pragma unroll
-                for (uint32_t c = 0; c < 2; ++c) {
+                for (uint32_t c = 0; c < kChunks; ++c) {
                     uint32_t dp[32], pk[16];
-                    tmem_ld32(tDP(buf) + kHalf * g + 32 * c + lane_field, dp);
+                    tmem_ld32(tDP(buf) + kCols * g + 32 * c + lane_field, dp);
                     tmem_wait_ld();
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
                         pk[e] = pack2<kBF16>(pr[32 * c + 2 * e] * (__uint_as_float(dp[2 * e]) - delta),
                                              pr[32 * c + 2 * e + 1] * (__uint_as_float(dp[2 * e + 1]) - delta));
-                    tmem_st16(tDP(buf) + kHalf * g + 16 * c + lane_field, pk);
+                    tmem_st16(tDP(buf) + kCols * g + 16 * c + lane_field, pk);
                 }
                 tmem_wait_st();
                 ew_arrive(&bars->ds_full);
             }
             if (!ok) break;
             if (!(ok = ew_wait(g, &bars->acc_full, acc_par, abort_flag))) break;
-            // epilogue: dQ columns [64g, 64g+64), scaled
+            // epilogue: dQ columns [kCols*g, kCols*(g+1)), scaled
             uint8_t* dq_row = static_cast<uint8_t*>(p.out0) + ridx * 128 * 2;
-            uint32_t acc[2][32];
-            tmem_ld32(tDQ + kHalf * g + lane_field, acc[0]);
-            tmem_ld32(tDQ + kHalf * g + 32 + lane_field, acc[1]);
+            uint32_t acc[kChunks][32];
+#pragma unroll
+            for (uint32_t c = 0; c < kChunks; ++c) tmem_ld32(tDQ + kCols * g + 32 * c + lane_field, acc[c]);
             tmem_wait_ld();
             ew_arrive(&bars->acc_empty);
             if (valid) {
 #pragma unroll
-                for (uint32_t c = 0; c < 2; ++c) {
+                for (uint32_t c = 0; c < kChunks; ++c) {
                     uint32_t pk[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
                         pk[e] = pack2<kBF16>(__uint_as_float(acc[c][2 * e]) * p.scale,
                                              __uint_as_float(acc[c][2 * e + 1]) * p.scale);
-                    uint4* dst = reinterpret_cast<uint4*>(dq_row + (kHalf * g + 32 * c) * 2);
+                    uint4* dst = reinterpret_cast<uint4*>(dq_row + (kCols * g + 32 * c) * 2);
 #pragma unroll
                     for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
                 }
@@ -717,41 +723,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ====== elementwise: P^T, dS^T, dK/dV epilogue (key = TMEM lane; warpgroup g = queries [64g, 64g+64)) ======
         const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
-        // this warpgroup's staging: [0..63] -lse*log2(e), [64..127] Delta
-        float* vec = reinterpret_cast<float*>(smem + kOffVec) + g * kBlk;
+        // this warpgroup's staging: [0, kCols) -lse*log2(e), [kCols, 2 kCols) Delta of its queries
+        float* vec = reinterpret_cast<float*>(smem + kOffVec) + g * 2 * kCols;
         uint32_t s_par = 0, dp_par = 0, acc_par = 0;
         Units u(blockIdx.x);
         uint32_t bh, kb;
         bool ok = true;
-        // on the diagonal block, query c of this half sees the key when 64g + c >= t
-        const int32_t first = static_cast<int32_t>(t) - static_cast<int32_t>(kHalf * g);
+        // on the diagonal block, query c of this warpgroup's columns sees the key when kCols*g + c >= t
+        const int32_t first = static_cast<int32_t>(t) - static_cast<int32_t>(kCols * g);
         while (ok && u.next(p, bh, kb)) {
             const uint32_t key = kb * kBlk + t;
             const size_t kidx = static_cast<size_t>(bh) * p.S_k + key;
             const uint32_t q0 = q_first_for(p, kb);
             if (q0 < nq) {
                 for (uint32_t i = q0; i < nq; ++i) {
-                    // stage -lse*log2(e) (-inf past S_q, so P = 0 there) and Delta of this half's 64
+                    // stage -lse*log2(e) (-inf past S_q, so P = 0 there) and Delta of this warpgroup's
                     // queries, once every thread of the group is done with the previous block's
-                    const uint32_t r = i * kBlk + kHalf * g + (t & 63);
+                    const uint32_t r = i * kBlk + kCols * g + (t % kCols);
                     const size_t ridx = static_cast<size_t>(bh) * p.S_q + r;
                     wg_sync(g);
-                    if (t < 64)
+                    if (t < kCols)
                         vec[t] = r < p.S_q ? -p.lse[ridx] * 1.4426950408889634f : -INFINITY;
-                    else
+                    else if (t < 2 * kCols)
                         vec[t] = r < p.S_q ? p.delta[ridx] : 0.f;
                     // phase 1: P^T from S^T, packed over it (the wait also publishes the staged values)
                     if (!(ok = ew_wait(g, &bars->s_full, s_par, abort_flag))) break;
-                    float pr[64];
+                    float pr[kCols];
                     {
-                        uint32_t s[64], pk[32];
-                        tmem_ld32(tS + kHalf * g + lane_field, *reinterpret_cast<uint32_t(*)[32]>(s));
-                        tmem_ld32(tS + kHalf * g + 32 + lane_field, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+                        uint32_t s[kCols], pk[kCols / 2];
+#pragma unroll
+                        for (uint32_t c = 0; c < kChunks; ++c)
+                            tmem_ld32(tS + kCols * g + 32 * c + lane_field, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c));
                         const float4* nl4 = reinterpret_cast<const float4*>(vec);
                         tmem_wait_ld();
                         if (p.causal && i == kb) {
 #pragma unroll
-                            for (int e4 = 0; e4 < 16; ++e4) {
+                            for (int e4 = 0; e4 < static_cast<int>(kCols / 4); ++e4) {
                                 const float4 nl = nl4[e4];
                                 const float nla[4] = {nl.x, nl.y, nl.z, nl.w};
 #pragma unroll
@@ -762,7 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                         } else {
 #pragma unroll
-                            for (int e4 = 0; e4 < 16; ++e4) {
+                            for (int e4 = 0; e4 < static_cast<int>(kCols / 4); ++e4) {
                                 const float4 nl = nl4[e4];
                                 const float nla[4] = {nl.x, nl.y, nl.z, nl.w};
 #pragma unroll
@@ -771,19 +778,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                             }
                         }
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) pk[e] = pack2<kBF16>(pr[2 * e], pr[2 * e + 1]);
-                        tmem_st16(tS + kHalf * g + lane_field, pk);
-                        tmem_st16(tS + kHalf * g + 16 + lane_field, pk + 16);
+                        for (int e = 0; e < static_cast<int>(kCols / 2); ++e) pk[e] = pack2<kBF16>(pr[2 * e], pr[2 * e + 1]);
+#pragma unroll
+                        for (uint32_t c = 0; c < kChunks; ++c) tmem_st16(tS + kCols * g + 16 * c + lane_field, pk + 16 * c);
                         tmem_wait_st();
                         ew_arrive(&bars->mid);
                     }
                     // phase 2: dS^T = P^T (dP^T - Delta), packed over dP^T
                     if (!(ok = ew_wait(g, &bars->dp_full[0], dp_par, abort_flag))) break;
 #pragma unroll
-                    for (uint32_t c = 0; c < 2; ++c) {
+                    for (uint32_t c = 0; c < kChunks; ++c) {
                         uint32_t dp[32], pk[16];
-                        tmem_ld32(tDP + kHalf * g + 32 * c + lane_field, dp);
-                        const float4* dl4 = reinterpret_cast<const float4*>(vec + 64 + 32 * c);
+                        tmem_ld32(tDP + kCols * g + 32 * c + lane_field, dp);
+                        const float4* dl4 = reinterpret_cast<const float4*>(vec + kCols + 32 * c);
                         tmem_wait_ld();
 #pragma unroll
                         for (int e4 = 0; e4 < 8; ++e4) {
@@ -794,7 +801,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             pk[2 * e4 + 1] = pack2<kBF16>(pr[b + 2] * (__uint_as_float(dp[4 * e4 + 2]) - dl.z),
                                                           pr[b + 3] * (__uint_as_float(dp[4 * e4 + 3]) - dl.w));
                         }
-                        tmem_st16(tDP + kHalf * g + 16 * c + lane_field, pk);
+                        tmem_st16(tDP + kCols * g + 16 * c + lane_field, pk);
                     }
                     tmem_wait_st();
                     ew_arrive(&bars->ds_full);
@@ -802,18 +809,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 if (!(ok = ew_wait(g, &bars->acc_full, acc_par, abort_flag))) break;
             }
-            // epilogue: dV, dK (scaled) of this key, columns [64g, 64g+64); zeros when no query sees the block
+            // epilogue: dV, dK (scaled) of this key, columns [kCols*g, kCols*(g+1)); zeros when no query sees the block
             const bool valid = key < p.S_k;
             uint8_t* dk_row = static_cast<uint8_t*>(p.out0) + kidx * 128 * 2;
             uint8_t* dv_row = static_cast<uint8_t*>(p.out1) + kidx * 128 * 2;
 #pragma unroll 1
-            for (uint32_t c = 0; c < 2; ++c) {
+            for (uint32_t c = 0; c < kChunks; ++c) {
                 uint32_t av[32], ak[32], pv[16], pk[16];
                 if (q0 < nq) {
-                    tmem_ld32(tDV + kHalf * g + 32 * c + lane_field, av);
-                    tmem_ld32(tDK + kHalf * g + 32 * c + lane_field, ak);
+                    tmem_ld32(tDV + kCols * g + 32 * c + lane_field, av);
+                    tmem_ld32(tDK + kCols * g + 32 * c + lane_field, ak);
                     tmem_wait_ld();
-                    if (c == 1) ew_arrive(&bars->acc_empty);  // the accumulators are read: the next unit may start them
+                    if (c + 1 == kChunks) ew_arrive(&bars->acc_empty);  // the accumulators are read: the next unit may start them
                 } else {
 #pragma unroll
                     for (int e = 0; e < 32; ++e) av[e] = ak[e] = 0u;
@@ -824,8 +831,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     pk[e] = pack2<kBF16>(__uint_as_float(ak[2 * e]) * p.scale, __uint_as_float(ak[2 * e + 1]) * p.scale);
                 }
                 if (valid) {
-                    uint4* dv = reinterpret_cast<uint4*>(dv_row + (kHalf * g + 32 * c) * 2);
-                    uint4* dk = reinterpret_cast<uint4*>(dk_row + (kHalf * g + 32 * c) * 2);
+                    uint4* dv = reinterpret_cast<uint4*>(dv_row + (kCols * g + 32 * c) * 2);
+                    uint4* dk = reinterpret_cast<uint4*>(dk_row + (kCols * g + 32 * c) * 2);
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
                         dv[v] = make_uint4(pv[4 * v], pv[4 * v + 1], pv[4 * v + 2], pv[4 * v + 3]);

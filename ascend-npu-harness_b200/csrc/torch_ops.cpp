@@ -19,6 +19,9 @@
 //   hc::rms_norm_rope_fused(x, weight, cos, sin, rotary_dim, eps, heads, rope_style)
 //   hc::matmul_bias(a, b, bias?)                                matmul_bias_runner.hpp
 //   hc::flash_attention_fwd_fused(q, k, v, scale, mask_type) -> (o, lse)   (k, v may have fewer heads: GQA)
+//   hc::flash_attention_bwd(q, k, v, o, lse, dout, scale, mask_type) -> (dq, dk, dv, delta)
+//                                          (no reference counterpart; K/V with the query head count)
+// hc.load_torch_ops() also registers the backward as the autograd formula of the forward op.
 // Load with torch.ops.load_library("ascend-npu-harness_b200/lib/libhc_torch.so").
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -247,6 +250,36 @@ std::tuple<at::Tensor, at::Tensor> flash_attention_fwd_fused_cuda(const at::Tens
     return {o, lse};
 }
 
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> flash_attention_bwd_cuda(
+    const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+    const at::Tensor& dout, double scale, int64_t mask_type) {
+    for (const auto& [t, n] : {std::pair<const at::Tensor&, const char*>{q, "q"}, {k, "k"}, {v, "v"}, {o, "o"},
+                               {dout, "dout"}})
+        check_input(t, n);
+    check_input(lse, "lse");
+    TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "hc: flash attention tensors are [B, H, S, D]");
+    TORCH_CHECK(k.sizes() == at::IntArrayRef({q.size(0), q.size(1), k.size(2), q.size(3)}) && v.size(0) == q.size(0) &&
+                    v.size(1) == q.size(1) && v.size(2) == k.size(2),
+                "hc: flash_attention_bwd needs K/V with the query head count and matching shapes");
+    TORCH_CHECK(o.sizes() == at::IntArrayRef({q.size(0), q.size(1), q.size(2), v.size(3)}) && dout.sizes() == o.sizes(),
+                "hc: flash_attention_bwd o / dout shape");
+    TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.sizes() == at::IntArrayRef({q.size(0), q.size(1), q.size(2)}),
+                "hc: flash_attention_bwd lse must be fp32 [B, H, S_q]");
+    for (const at::Tensor* t : {&k, &v, &o, &dout})
+        TORCH_CHECK(t->scalar_type() == q.scalar_type(), "hc: flash_attention_bwd tensors must share a dtype");
+    c10::cuda::CUDAGuard guard(q.device());
+    at::Tensor dq = at::empty_like(q), dk = at::empty_like(k), dv = at::empty_like(v);
+    at::Tensor delta = at::empty({q.size(0), q.size(1), q.size(2)}, q.options().dtype(at::kFloat));
+    flash_attention_fwd_fused_tiling_data t{u32(q.size(0), "B"), u32(q.size(1), "H"), u32(q.size(2), "S_q"),
+                                            u32(k.size(2), "S_k"), u32(q.size(3), "D"), u32(v.size(3), "D_v"),
+                                            static_cast<float>(scale), u32(mask_type, "mask_type")};
+    ok_or_throw(hc_flash_attention_bwd_launch(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), dout.data_ptr(),
+                                              lse.data_ptr<float>(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                              delta.data_ptr<float>(), &t, dtype_code(q), stream_of(q)),
+                "flash_attention_bwd");
+    return {dq, dk, dv, delta};
+}
+
 // ---------------------------------------------------------------------------------------------
 // Meta kernels (shapes only)
 // ---------------------------------------------------------------------------------------------
@@ -280,6 +313,13 @@ std::tuple<at::Tensor, at::Tensor> flash_attention_fwd_fused_meta(const at::Tens
             at::empty({q.size(0), q.size(1), q.size(2)}, q.options().dtype(at::kFloat))};
 }
 
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor> flash_attention_bwd_meta(
+    const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor&, const at::Tensor&,
+    const at::Tensor&, double, int64_t) {
+    return {at::empty_like(q), at::empty_like(k), at::empty_like(v),
+            at::empty({q.size(0), q.size(1), q.size(2)}, q.options().dtype(at::kFloat))};
+}
+
 }  // namespace
 
 TORCH_LIBRARY(hc, m) {
@@ -294,6 +334,8 @@ TORCH_LIBRARY(hc, m) {
           "int heads=1, int rope_style=0) -> Tensor");
     m.def("matmul_bias(Tensor a, Tensor b, Tensor? bias=None) -> Tensor");
     m.def("flash_attention_fwd_fused(Tensor q, Tensor k, Tensor v, float scale, int mask_type) -> (Tensor, Tensor)");
+    m.def("flash_attention_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, Tensor dout, float scale, "
+          "int mask_type) -> (Tensor, Tensor, Tensor, Tensor)");
 }
 
 TORCH_LIBRARY_IMPL(hc, CUDA, m) {
@@ -307,6 +349,7 @@ TORCH_LIBRARY_IMPL(hc, CUDA, m) {
     m.impl("rms_norm_rope_fused", &rms_norm_rope_fused_cuda);
     m.impl("matmul_bias", &matmul_bias_cuda);
     m.impl("flash_attention_fwd_fused", &flash_attention_fwd_fused_cuda);
+    m.impl("flash_attention_bwd", &flash_attention_bwd_cuda);
 }
 
 TORCH_LIBRARY_IMPL(hc, Meta, m) {
@@ -320,4 +363,5 @@ TORCH_LIBRARY_IMPL(hc, Meta, m) {
     m.impl("rms_norm_rope_fused", &rms_norm_rope_fused_meta);
     m.impl("matmul_bias", &matmul_bias_meta);
     m.impl("flash_attention_fwd_fused", &flash_attention_fwd_fused_meta);
+    m.impl("flash_attention_bwd", &flash_attention_bwd_meta);
 }

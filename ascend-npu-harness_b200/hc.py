@@ -367,15 +367,43 @@ _torch_ops_loaded = False
 
 def load_torch_ops():
     """Registers the `hc` torch custom ops (lib/libhc_torch.so, csrc/torch_ops.cpp) and returns torch.ops.hc.
-    The ops call the same C ABI as this module, on the current CUDA stream; they raise on CPU tensors."""
+    The ops call the same C ABI as this module, on the current CUDA stream; they raise on CPU tensors.
+    hc::flash_attention_fwd_fused gets an autograd formula: hc::flash_attention_bwd (q, k, v get
+    gradients; the lse output is not differentiable)."""
     global _torch_ops_loaded
     torch = _torch()
     if not _torch_ops_loaded:
         if not TORCH_OPS_PATH.exists():
             raise HcError(HC_ERR_INVALID, f"{TORCH_OPS_PATH} is missing; run ascend-npu-harness_b200/build.py")
         torch.ops.load_library(str(TORCH_OPS_PATH))
+        torch.library.register_autograd("hc::flash_attention_fwd_fused", _fa_backward, setup_context=_fa_setup)
         _torch_ops_loaded = True
     return torch.ops.hc
+
+
+def _fa_setup(ctx, inputs, output):
+    q, k, v, scale, mask_type = inputs
+    o, lse = output
+    ctx.save_for_backward(q, k, v, o, lse)
+    ctx.scale, ctx.mask_type = scale, mask_type
+    ctx.mark_non_differentiable(lse)
+
+
+def _fa_backward(ctx, grad_o, grad_lse):
+    """Gradients of hc::flash_attention_fwd_fused through hc::flash_attention_bwd.  Grouped-query K/V
+    (fewer heads) are expanded to the query heads for the kernel and their gradients summed back
+    over each group (query head h reads K/V head h // (H / kv_heads), as in the forward)."""
+    torch = _torch()
+    q, k, v, o, lse = ctx.saved_tensors
+    H, kv = q.shape[1], k.shape[1]
+    group = H // kv
+    ke, ve = (k, v) if group == 1 else (k.repeat_interleave(group, 1), v.repeat_interleave(group, 1))
+    dq, dk, dv, _ = torch.ops.hc.flash_attention_bwd(q, ke.contiguous(), ve.contiguous(), o, lse,
+                                                      grad_o.contiguous(), ctx.scale, ctx.mask_type)
+    if group > 1:
+        dk = dk.view(k.shape[0], kv, group, *k.shape[2:]).sum(2)
+        dv = dv.view(v.shape[0], kv, group, *v.shape[2:]).sum(2)
+    return dq, dk, dv, None, None
 
 
 def check_device_error() -> None:

@@ -1,5 +1,6 @@
 """The `hc` torch custom-op library (csrc/torch_ops.cpp): registration and shape inference on CPU,
-results on the GPU identical to the ctypes binding (both call the same C ABI)."""
+results on the GPU identical to the ctypes binding (both call the same C ABI), and autograd through
+hc::flash_attention_fwd_fused (the backward kernels) against an fp32 torch restatement."""
 from __future__ import annotations
 
 import math
@@ -15,7 +16,8 @@ sys.path.insert(0, str(ROOT / "ascend-npu-harness_b200"))
 import hc  # noqa: E402
 
 OPS = ("elementwise_add", "axpy_scalar_affine", "broadcast_binary", "activation_gelu_silu", "reduce_sum_lastdim",
-       "transpose_2d_4d", "layer_norm", "rms_norm_rope_fused", "matmul_bias", "flash_attention_fwd_fused")
+       "transpose_2d_4d", "layer_norm", "rms_norm_rope_fused", "matmul_bias", "flash_attention_fwd_fused",
+       "flash_attention_bwd")
 
 
 @pytest.fixture(scope="module")
@@ -70,6 +72,9 @@ def test_meta_shapes(ops):
     assert ops.flash_attention_fwd_fused(q6, kv, kv, 0.088, 1)[0].shape == (2, 6, 100, 128)
     with pytest.raises(RuntimeError, match="must divide"):
         ops.flash_attention_fwd_fused(torch.empty(2, 4, 100, 128, dtype=torch.bfloat16, **m), kv, kv, 0.088, 1)
+    dq, dk, dv, delta = ops.flash_attention_bwd(q, kv, kv, o, lse, o, 0.088, 1)
+    assert dq.shape == q.shape and dk.shape == kv.shape and dv.shape == kv.shape
+    assert delta.shape == (2, 3, 100) and delta.dtype == torch.float32
 
 
 def test_cpu_tensors_have_no_kernel(ops):
@@ -123,7 +128,56 @@ def test_ops_match_ctypes_binding(ops):
     o, lse = ops.flash_attention_fwd_fused(q, kg, vg, 1 / math.sqrt(128), 1)
     o2, lse2 = hc.flash_attention_fwd(q, kg, vg, True)
     assert eq(o, o2) and torch.equal(lse, lse2)
+    dout = rnd(1, 4, 300, 128)
+    o, lse = hc.flash_attention_fwd(q, k, v, True)
+    g1 = ops.flash_attention_bwd(q, k, v, o, lse, dout, 1 / math.sqrt(128), 1)
+    g2 = hc.flash_attention_bwd(q, k, v, o, lse, dout, True)
+    assert all(eq(a, b) for a, b in zip(g1[:3], g2[:3])) and torch.equal(g1[3], g2[3])
     torch.cuda.synchronize()
+    hc.check_device_error()
+
+
+def _reference_grads(q, k, v, dout, scale, causal):
+    """fp32 gradients of softmax(q k^T * scale [causal]) v by torch autograd (no TF32); K/V heads
+    repeated for grouped-query inputs."""
+    import torch
+
+    group = q.shape[1] // k.shape[1]
+    qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    s = (qf @ kf.repeat_interleave(group, 1).transpose(-1, -2)) * scale
+    if causal:
+        s = s.masked_fill(torch.ones(s.shape[-2:], dtype=torch.bool, device=s.device).triu(1), float("-inf"))
+    (torch.softmax(s, -1) @ vf.repeat_interleave(group, 1)).backward(dout.float())
+    return qf.grad, kf.grad, vf.grad
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("causal", [True, False], ids=["causal", "none"])
+@pytest.mark.parametrize("kv_heads", [4, 2], ids=["mha", "gqa"])
+def test_flash_attention_autograd(ops, causal, kv_heads):
+    """loss.backward() through hc::flash_attention_fwd_fused runs the tcgen05 backward kernels; the
+    gradients match fp32 autograd of the same attention (normwise 1e-2, the bf16 backward bound)."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(3)
+    rnd = lambda *s: torch.randn(*s, generator=g, device="cuda").to(torch.bfloat16)  # noqa: E731
+    q = rnd(2, 4, 384, 128).requires_grad_(True)
+    k, v = (rnd(2, kv_heads, 384, 128).requires_grad_(True) for _ in range(2))
+    dout = rnd(2, 4, 384, 128)
+    scale = 1 / math.sqrt(128)
+    o, _ = ops.flash_attention_fwd_fused(q, k, v, scale, 1 if causal else 0)
+    o.backward(dout)
+    assert hc.load().hc_flash_attention_bwd_last_path() == 1
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        ref = _reference_grads(q, k, v, dout, scale, causal)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    for name, got, exp in zip(("dq", "dk", "dv"), (q.grad, k.grad, v.grad), ref):
+        assert got.shape == exp.shape and got.dtype == torch.bfloat16
+        err = float((got.float() - exp).norm() / exp.norm())
+        assert err <= 1e-2, f"{name}: normwise {err:.3g}"
     hc.check_device_error()
 
 
