@@ -80,6 +80,31 @@ def test_16bit_tolerances_match_the_gpu_tests():
         assert all(specs.tolerance(op, dt).get("bit_exact") for dt in ("bfloat16", "float16", "float32")), op
 
 
+def test_backward_contract():
+    """The flash-attention backward block of spec 10: entry point in the C ABI, kernels in the
+    sources, tolerances equal to the GPU tests', bench configuration and FLOP ratio equal to bench.py's."""
+    import test_gpu_flash_attention_bwd as bwd
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    b = specs.spec("flash_attention_fwd_fused")["backward"]
+    header = (ROOT / "include" / "hc_ops.h").read_text()
+    for ep in b["entry_points"]:
+        assert re.search(rf"\b{ep}\s*\(", header), ep
+    src = "".join(p.read_text() for p in (ROOT / "ascend-npu-harness_b200" / "csrc").glob("*.cu"))
+    for k in b["kernels"]:
+        assert re.search(rf"\b{k['name']}\s*\(", src), k["name"]
+    for dt, key in (("bfloat16", "bf16"), ("float16", "f16"), ("float32", "f32")):
+        assert (b["accuracy"][dt]["normwise"], b["accuracy"][dt]["max_abs_of_max"]) == bwd.BWD_TOL[key]
+    assert b["accuracy"]["bfloat16"]["normwise"] == bench.FA_BWD_TOL
+    assert bench.FA_BWD_FLOP_RATIO == 2.5
+    c = b["benchmark"]["config"]
+    assert (c["B"], c["H"], c["S_q"], c["D"]) == (bench.FA_B, bench.FA_H, bench.FA_S, bench.FA_D)
+    for f in b["tests"]["files"]:
+        assert (ROOT / f).exists(), f
+
+
 def test_benchmark_configurations_are_the_named_workloads():
     fa = specs.bench_config("flash_attention_fwd_fused")
     assert (fa["B"], fa["H"], fa["S_q"], fa["S_k"], fa["D"], fa["D_v"]) == (16, 32, 8192, 8192, 128, 128)
