@@ -19,10 +19,10 @@
 //     P^T (16-bit, over S^T), dS^T (16-bit, over dP^T), dV += P^T dO_i, dK += dS^T Q_i.
 //     TMEM: S^T [0,128), dP^T [128,256), dV [256,384), dK [384,512).
 // Every product is M=128, N=128, K=16 per instruction: one tcgen05.mma every 64 cycles at the full
-// tensor rate (N = 64 runs at two thirds of it, bound by shared-memory operand reads).  The two
-// elementwise warpgroups (warps 0-3 and 4-7; a thread owns one TMEM lane, warpgroup g the 64 columns
-// [64g, 64g+64) of each tile) work in two phases per block, each with its own hand-off to the MMA
-// warp (warp 8), which keeps the tensor pipe busy during both:
+// tensor rate (N = 64 runs at two thirds of it, bound by shared-memory operand reads).  The kWG
+// elementwise warpgroups (warps 4g..4g+3; a thread owns one TMEM lane, warpgroup g the kCols columns
+// [kCols*g, kCols*(g+1)) of each tile) work in two phases per block, each with its own hand-off to
+// the MMA warp (warp 4*kWG), which keeps the tensor pipe busy during both:
 //   dQ:    phase 1 loads S and releases it (the next S is issued at once), forms P in registers;
 //          phase 2 forms dS from dP and packs it over dP (ds_full): dQ += dS K_j, then dP of block
 //          j + 2 into the same buffer, so phase 2 of the next block never waits for this product.
@@ -30,7 +30,7 @@
 //          S^T; phase 2 forms dS^T and packs it over dP^T (ds_full): dK += dS^T Q_i, then the next
 //          dP^T.
 // The accumulators of the next work unit are started only after both warpgroups' epilogues have
-// read them (acc_empty).  Warp 9 issues TMA (no multicast).  The causal mask is applied only on the
+// read them (acc_empty).  Warp 4*kWG+1 issues TMA (no multicast).  The causal mask is applied only on the
 // diagonal block; tails need none (rows past S_q get lse = +inf, so P = 0; keys past S_k meet zero
 // K/V rows or land in accumulator rows that are not stored).  Work units are handed out as
 // complementary block pairs (b, n-1-b) of one head so that every CTA gets the same causal work.
@@ -72,7 +72,7 @@ constexpr uint32_t kStages = 5;                 // streamed-tile ring (tiles are
 constexpr uint32_t kOffFixed = 0;               // two tiles resident per unit (Q,dO or K,V)
 constexpr uint32_t kOffRing = 2 * kTileBytes;
 constexpr uint32_t kOffBar = kOffRing + kStages * kTileBytes;
-constexpr uint32_t kOffVec = kOffBar + 256;     // dK/dV: per warpgroup, -lse*log2(e) and Delta of its 64 queries
+constexpr uint32_t kOffVec = kOffBar + 256;     // dK/dV: per warpgroup, -lse*log2(e) and Delta of its kCols queries
 constexpr uint32_t kVecBytes = kWG * 2 * kCols * 4;
 constexpr uint32_t kSmemBytes = kOffVec + kVecBytes + 1024;
 
@@ -99,7 +99,7 @@ struct Bars {
     uint64_t fixed_full, fixed_empty;
     uint64_t ring_full[kStages], ring_empty[kStages];
     uint64_t s_full, dp_full[2];   // MMA -> elementwise: S (S^T) and dP (dP^T, buffer b) of the block are in TMEM
-    uint64_t mid, ds_full;         // elementwise -> MMA (256 arrivals): phase 1 done (dQ: S read; dK/dV: P^T packed), phase 2 (dS packed)
+    uint64_t mid, ds_full;         // elementwise -> MMA (kElem arrivals): phase 1 done (dQ: S read; dK/dV: P^T packed), phase 2 (dS packed)
     uint64_t acc_full, acc_empty;
     uint64_t mma_done;
 };
@@ -150,28 +150,6 @@ template <bool kBF16>
 __device__ __forceinline__ float2 unpack2(uint32_t w) {
     if (kBF16) return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
     return __half22float2(*reinterpret_cast<const __half2*>(&w));
-}
-
-// D (M=128, N=128) = A (128 x 128, K-major smem) * B^T (128 x 128, K-major smem): 8 K-steps of 16.
-__device__ __forceinline__ void issue_ss(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr, uint32_t idesc) {
-    const Sw128Desc ad = make_sw128_desc2(a_addr, 16, 1024), bd = make_sw128_desc2(b_addr, 16, 1024);
-#pragma unroll
-    for (uint32_t kk = 0; kk < 8; ++kk) {
-        const uint32_t off = ((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4;
-        mma_ss2(d_tmem, Sw128Desc{ad.lo + off, ad.hi}, Sw128Desc{bd.lo + off, bd.hi}, idesc, kk > 0);
-    }
-}
-
-// D (M=128, N=128) (+)= A * B with B a 128-row MN-major smem tile (K along its rows) and A a 128 x 128
-// 16-bit tile in TMEM packed by the two warpgroups: K range [64g, 64g+64) in columns [64g, 64g+32)
-// from `a_tmem`.  `accumulate` false starts D afresh.
-__device__ __forceinline__ void issue_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, uint32_t idesc,
-                                         bool accumulate) {
-    const Sw128Desc bd = make_sw128_desc2(b_addr, kPanelBytes, 1024);
-#pragma unroll
-    for (uint32_t kk = 0; kk < 8; ++kk)
-        mma_ts2(d_tmem, a_tmem + (kk / kStepsWG) * kCols + (kk % kStepsWG) * 8, Sw128Desc{bd.lo + kk * (2048 >> 4), bd.hi}, idesc,
-                (accumulate || kk > 0) ? 1u : 0u);
 }
 
 __device__ __forceinline__ uint32_t n_blocks(uint32_t S) { return (S + kBlk - 1) / kBlk; }
@@ -288,38 +266,15 @@ struct Ring {
     }
 };
 
-// The MMA warp's consumer side of the ring, in the producer's order.
+// The MMA warp's position in the ring (consumed in the producer's order by Issuer::ring_one).
 struct RingWait {
     uint32_t stage = 0, phase = 0;
-    __device__ __forceinline__ bool one(Bars* bars, volatile uint32_t* abort_flag, uint32_t& st) {
-        if (!mbar_wait_bounded(&bars->ring_full[stage], phase, abort_flag, &g_fab_error_word, kErrMma)) return false;
-        tc_fence_after();
-        st = stage;
-        if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1;
-        }
-        return true;
-    }
 };
 
 // Per-thread parities of the MMA warp's waits, kept across units.
 struct MmaPar {
     uint32_t mid = 0, ds = 0;
 };
-
-__device__ __forceinline__ bool mma_wait(uint64_t* bar, uint32_t& par, volatile uint32_t* abort_flag) {
-    if (!mbar_wait_bounded(bar, par, abort_flag, &g_fab_error_word, kErrMma)) return false;
-    par ^= 1;
-    tc_fence_after();
-    return true;
-}
-
-__device__ __forceinline__ void mma_finish(Bars* bars) {
-    tc_commit(&bars->mma_done);
-    volatile uint32_t never = 0;
-    mbar_wait_bounded(&bars->mma_done, 0, &never, &g_fab_error_word, kErrDrain, 1000000000ull);
-}
 
 // The MMA warp runs converged: every lane computes the same descriptors and waits on the same
 // barriers (their give-up decisions ANDed over the warp), and only the elected lane issues the
@@ -365,7 +320,7 @@ struct Issuer {
             "r"(a_tmem), "r"(b.lo), "r"(b.hi), "r"(idesc), "r"(acc), "r"(leader)
             : "memory");
     }
-    // the products of issue_ss / issue_ts
+    // D (M=128, N=128) = A (128 x 128, K-major smem) * B^T (128 x 128, K-major smem): 8 K-steps of 16.
     __device__ __forceinline__ void ss(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr, uint32_t idesc) const {
         const Sw128Desc ad = make_sw128_desc2(a_addr, 16, 1024), bd = make_sw128_desc2(b_addr, 16, 1024);
 #pragma unroll
@@ -374,6 +329,9 @@ struct Issuer {
             mma_ss(d_tmem, Sw128Desc{ad.lo + off, ad.hi}, Sw128Desc{bd.lo + off, bd.hi}, idesc, kk > 0);
         }
     }
+    // D (M=128, N=128) (+)= A * B with B a 128-row MN-major smem tile (K along its rows) and A a
+    // 128 x 128 16-bit tile in TMEM packed by the warpgroups: K range [kCols*g, kCols*(g+1)) in
+    // columns [kCols*g, kCols*g + kCols/2) from `a_tmem`.  `accumulate` false starts D afresh.
     __device__ __forceinline__ void ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, uint32_t idesc,
                                        bool accumulate) const {
         const Sw128Desc bd = make_sw128_desc2(b_addr, kPanelBytes, 1024);
@@ -514,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             is.finish(bars);
         }
     } else {
-        // ====== elementwise: Delta, P, dS, dQ epilogue (row = TMEM lane; warpgroup g = keys [64g, 64g+64)) ======
+        // ====== elementwise: Delta, P, dS, dQ epilogue (row = TMEM lane; warpgroup g = keys [kCols*g, kCols*(g+1))) ======
         const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
         const uint8_t* tDOs = smem + kOffFixed + kTileBytes;
@@ -720,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             is.finish(bars);
         }
     } else {
-        // ====== elementwise: P^T, dS^T, dK/dV epilogue (key = TMEM lane; warpgroup g = queries [64g, 64g+64)) ======
+        // ====== elementwise: P^T, dS^T, dK/dV epilogue (key = TMEM lane; warpgroup g = queries [kCols*g, kCols*(g+1))) ======
         const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
         // this warpgroup's staging: [0, kCols) -lse*log2(e), [kCols, 2 kCols) Delta of its queries
