@@ -1,4 +1,4 @@
-"""The FMA-pipe exponential of the flash-attention softmax (exp2_poly2 in ops_attention.cu):
+"""The FMA-pipe exponential of the flash-attention softmax (exp2_poly2 in exp2_poly.cuh):
 its constants are the Remez minimax fit that tests/exp2_poly_fit.py derives, and the exact fp32
 device sequence (emulated here) stays within 1e-4 relative error of 2^x on the range the kernel
 uses it for.  CPU only."""
@@ -17,7 +17,7 @@ import exp2_poly_fit as fit  # noqa: E402
 
 
 def kernel_constants():
-    src = (ROOT / "ascend-npu-harness_b200" / "csrc" / "ops_attention.cu").read_text()
+    src = (ROOT / "ascend-npu-harness_b200" / "csrc" / "exp2_poly.cuh").read_text()
     return [float(re.search(rf"kExp2C{i} = ([0-9.eE+-]+)f;", src).group(1)) for i in range(4)]
 
 
