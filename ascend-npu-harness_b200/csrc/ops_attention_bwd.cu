@@ -4,8 +4,8 @@
 //   P = exp(S * scale - lse), dV = P^T dO, dP = dO V^T, Delta = rowsum(dO * O),
 //   dS = P * (dP - Delta), dQ = scale * dS K, dK = scale * dS^T Q.
 //
-// Tensor-core path (bf16/fp16, D = D_v = 128, 16-byte aligned buffers): two kernels with the same
-// structure.  A CTA holds two 128 x 128 "fixed" tiles of one 128-row block in shared memory and
+// Tensor-core path (bf16/fp16, D = D_v = 64 or 128, 16-byte aligned buffers): two kernels with the same
+// structure.  A CTA holds two 128 x D "fixed" tiles of one 128-row block in shared memory and
 // streams the other side's 128-row tiles through a 5-stage TMA ring.  Each streamed tile is released
 // as soon as its last product is issued (V_j and dO_i after one product, K_j and Q_i after two), and
 // the MMA warp waits for each tile just before its first product, so loads run about a block ahead:
@@ -60,7 +60,6 @@ using namespace sm100;
 
 constexpr uint32_t kBlk = 128;                  // rows (queries or keys) per block
 constexpr uint32_t kPanelBytes = 128 * 64 * 2;  // one 64-column swizzle panel of a 128-row tile: 16 KB
-constexpr uint32_t kTileBytes = 2 * kPanelBytes;  // a 128 x 128 16-bit tile: 32 KB
 constexpr uint32_t kWG = 2;                     // elementwise warpgroups
 constexpr uint32_t kCols = kBlk / kWG;          // columns of a tile per warpgroup
 constexpr uint32_t kChunks = kCols / 32;        // 32-column TMEM loads per thread and tile
@@ -70,11 +69,24 @@ constexpr uint32_t kMmaWarp = 4 * kWG, kTmaWarp = 4 * kWG + 1;
 constexpr uint32_t kThreads = kElem + 64;       // elementwise warpgroups, the MMA warp, the TMA warp
 constexpr uint32_t kStages = 5;                 // streamed-tile ring (tiles are released one by one)
 constexpr uint32_t kOffFixed = 0;               // two tiles resident per unit (Q,dO or K,V)
-constexpr uint32_t kOffRing = 2 * kTileBytes;
-constexpr uint32_t kOffBar = kOffRing + kStages * kTileBytes;
-constexpr uint32_t kOffVec = kOffBar + 256;     // dK/dV: per warpgroup, -lse*log2(e) and Delta of its kCols queries
 constexpr uint32_t kVecBytes = kWG * 2 * kCols * 4;
-constexpr uint32_t kSmemBytes = kOffVec + kVecBytes + 1024;
+
+// Shared-memory layout and epilogue split for head dim HD (64 or 128; D = D_v): a 128-row tile is
+// HD/64 swizzle panels; the ring follows the two fixed tiles; dQ / dK / dV rows are written
+// kOutCols columns per warpgroup.
+template <uint32_t HD>
+struct Dims {
+    static_assert(HD == 64 || HD == 128, "head dims 64 and 128");
+    static constexpr uint32_t kPanels = HD / 64;
+    static constexpr uint32_t kTileBytes = kPanels * kPanelBytes;
+    static constexpr uint32_t kOffRing = 2 * kTileBytes;
+    static constexpr uint32_t kOffBar = kOffRing + kStages * kTileBytes;
+    static constexpr uint32_t kOffVec = kOffBar + 256;  // dK/dV: per warpgroup, -lse*log2(e) and Delta of its kCols queries
+    static constexpr uint32_t kSmemBytes = kOffVec + kVecBytes + 1024;
+    static constexpr uint32_t kOutCols = HD / kWG;
+    static constexpr uint32_t kOutChunks = kOutCols / 32;
+    static_assert(kOutCols % 32 == 0, "32-column TMEM loads per warpgroup");
+};
 
 enum : uint32_t {
     kErrProducer = 1u << 0,
@@ -238,14 +250,16 @@ __device__ __forceinline__ void teardown_cta(uint32_t tmem_base, uint32_t warp) 
 // issued load is waited for (bounded) so no copy lands in shared memory after the CTA exits.
 struct Ring {
     uint32_t stage = 0, phase = 0, pend_valid = 0, pend_phase = 0;
+    template <uint32_t HD>
     __device__ __forceinline__ bool load(Bars* bars, uint8_t* smem, const CUtensorMap* tm, uint32_t row_blk,
                                          uint32_t bh, volatile uint32_t* abort_flag) {
+        using D = Dims<HD>;
         if (!mbar_wait_bounded(&bars->ring_empty[stage], phase ^ 1, abort_flag, &g_fab_error_word, kErrProducer))
             return false;
-        mbar_arrive_expect_tx(&bars->ring_full[stage], kTileBytes);
-        for (uint32_t h = 0; h < 2; ++h)
-            tma_load_3d(smem + kOffRing + stage * kTileBytes + h * kPanelBytes, tm, &bars->ring_full[stage], h * 64,
-                        row_blk * kBlk, bh);
+        mbar_arrive_expect_tx(&bars->ring_full[stage], D::kTileBytes);
+        for (uint32_t h = 0; h < D::kPanels; ++h)
+            tma_load_3d(smem + D::kOffRing + stage * D::kTileBytes + h * kPanelBytes, tm, &bars->ring_full[stage],
+                        h * 64, row_blk * kBlk, bh);
         pend_valid |= 1u << stage;
         pend_phase = (pend_phase & ~(1u << stage)) | (phase << stage);
         if (++stage == kStages) {
@@ -320,16 +334,17 @@ struct Issuer {
             "r"(a_tmem), "r"(b.lo), "r"(b.hi), "r"(idesc), "r"(acc), "r"(leader)
             : "memory");
     }
-    // D (M=128, N=128) = A (128 x 128, K-major smem) * B^T (128 x 128, K-major smem): 8 K-steps of 16.
+    // D (M=128, N=128) = A (128 x HD, K-major smem) * B^T (128 x HD, K-major smem): HD/16 K-steps.
+    template <uint32_t HD>
     __device__ __forceinline__ void ss(uint32_t d_tmem, uint32_t a_addr, uint32_t b_addr, uint32_t idesc) const {
         const Sw128Desc ad = make_sw128_desc2(a_addr, 16, 1024), bd = make_sw128_desc2(b_addr, 16, 1024);
 #pragma unroll
-        for (uint32_t kk = 0; kk < 8; ++kk) {
+        for (uint32_t kk = 0; kk < HD / 16; ++kk) {
             const uint32_t off = ((kk >> 2) * kPanelBytes + (kk & 3) * 32) >> 4;
             mma_ss(d_tmem, Sw128Desc{ad.lo + off, ad.hi}, Sw128Desc{bd.lo + off, bd.hi}, idesc, kk > 0);
         }
     }
-    // D (M=128, N=128) (+)= A * B with B a 128-row MN-major smem tile (K along its rows) and A a
+    // D (M=128, N=HD) (+)= A * B with B a 128-row MN-major smem tile (K along its rows) and A a
     // 128 x 128 16-bit tile in TMEM packed by the warpgroups: K range [kCols*g, kCols*(g+1)) in
     // columns [kCols*g, kCols*g + kCols/2) from `a_tmem`.  `accumulate` false starts D afresh.
     __device__ __forceinline__ void ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_addr, uint32_t idesc,
@@ -373,19 +388,20 @@ __device__ __forceinline__ void ew_arrive(uint64_t* bar) {
 // ============================================================================================
 // dQ (and Delta)
 // ============================================================================================
-template <bool kBF16>
+template <bool kBF16, uint32_t HD>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                      const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                      const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + sizeof(Bars));
+    using D = Dims<HD>;
+    Bars* bars = reinterpret_cast<Bars*>(smem + D::kOffBar);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + D::kOffBar + sizeof(Bars));
     volatile uint32_t* abort_flag = tmem_slot + 1;
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const uint32_t tmem_base = setup_cta(bars, tmem_slot, abort_flag, warp);
-    const uint32_t sQ = smem_u32(smem + kOffFixed), sDO = sQ + kTileBytes, sRing = smem_u32(smem + kOffRing);
+    const uint32_t sQ = smem_u32(smem + kOffFixed), sDO = sQ + D::kTileBytes, sRing = smem_u32(smem + D::kOffRing);
     const uint32_t tS = tmem_base, tDQ = tmem_base + 384;
     auto tDP = [&](uint32_t b) { return tmem_base + 128 + 128 * b; };
     if (warp == kTmaWarp) {
@@ -401,18 +417,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&bars->fixed_full, 2 * kTileBytes);
-                for (uint32_t h = 0; h < 2; ++h) {
+                mbar_arrive_expect_tx(&bars->fixed_full, 2 * D::kTileBytes);
+                for (uint32_t h = 0; h < D::kPanels; ++h) {
                     tma_load_3d(smem + kOffFixed + h * kPanelBytes, &tm_q, &bars->fixed_full, h * 64, qb * kBlk, bh);
-                    tma_load_3d(smem + kOffFixed + kTileBytes + h * kPanelBytes, &tm_do, &bars->fixed_full, h * 64,
+                    tma_load_3d(smem + kOffFixed + D::kTileBytes + h * kPanelBytes, &tm_do, &bars->fixed_full, h * 64,
                                 qb * kBlk, bh);
                 }
                 fixed_pending = static_cast<int32_t>(it & 1);
                 const uint32_t nkv = kv_blocks_for(p, qb);
                 // the MMA warp's order: K_0, V_0, then V_m ahead of K_m (dP runs a block ahead of S)
-                ok = ring.load(bars, smem, &tm_k, 0, bh, abort_flag) && ring.load(bars, smem, &tm_v, 0, bh, abort_flag);
+                ok = ring.template load<HD>(bars, smem, &tm_k, 0, bh, abort_flag) && ring.template load<HD>(bars, smem, &tm_v, 0, bh, abort_flag);
                 for (uint32_t m = 1; m < nkv && ok; ++m)
-                    ok = ring.load(bars, smem, &tm_v, m, bh, abort_flag) && ring.load(bars, smem, &tm_k, m, bh, abort_flag);
+                    ok = ring.template load<HD>(bars, smem, &tm_v, m, bh, abort_flag) && ring.template load<HD>(bars, smem, &tm_k, m, bh, abort_flag);
             }
             if (!ok) ring.drain(bars, fixed_pending);
         }
@@ -420,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         {
             const Issuer is{elect_one() ? 1u : 0u};
             const uint32_t idesc_ss = make_idesc_f16(kBF16, 128, 128, false, false);
-            const uint32_t idesc_ts = make_idesc_f16(kBF16, 128, 128, false, true);
+            const uint32_t idesc_ts = make_idesc_f16(kBF16, 128, HD, false, true);
             RingWait ring;
             MmaPar par;
             uint32_t it = 0;
@@ -432,12 +448,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 uint32_t ks, vs;
                 if (!is.ring_one(ring, bars, abort_flag, ks)) break;
-                is.ss(tS, sQ, sRing + ks * kTileBytes, idesc_ss);             // S_0 = Q K_0^T
+                is.template ss<HD>(tS, sQ, sRing + ks * D::kTileBytes, idesc_ss);             // S_0 = Q K_0^T
                 is.commit(&bars->s_full);
                 bool ok = true;
                 for (uint32_t b = 0; b < 2 && b < n && ok; ++b) {                // dP_0, dP_1 = dO V_b^T
                     if (!is.ring_one(ring, bars, abort_flag, vs)) { ok = false; break; }
-                    is.ss(tDP(b), sDO, sRing + vs * kTileBytes, idesc_ss);
+                    is.template ss<HD>(tDP(b), sDO, sRing + vs * D::kTileBytes, idesc_ss);
                     is.commit(&bars->dp_full[b]);
                     is.commit(&bars->ring_empty[vs]);                            // V has no other reader
                 }
@@ -450,16 +466,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!is.wait_flip(&bars->mid, par.mid, abort_flag)) { ok = false; break; }
                     if (nxt) {
                         if (!is.ring_one(ring, bars, abort_flag, kn)) { ok = false; break; }
-                        is.ss(tS, sQ, sRing + kn * kTileBytes, idesc_ss);
+                        is.template ss<HD>(tS, sQ, sRing + kn * D::kTileBytes, idesc_ss);
                         is.commit(&bars->s_full);
                     }
                     // dS_j packed over dP_j: dQ += dS_j K_j, then dP_{j+2} into that buffer
                     if (!is.wait_flip(&bars->ds_full, par.ds, abort_flag)) { ok = false; break; }
-                    is.ts(tDQ, tDP(j & 1), sRing + ks * kTileBytes, idesc_ts, j > 0);
+                    is.ts(tDQ, tDP(j & 1), sRing + ks * D::kTileBytes, idesc_ts, j > 0);
                     is.commit(&bars->ring_empty[ks]);
                     if (j + 2 < n) {
                         if (!is.ring_one(ring, bars, abort_flag, vn)) { ok = false; break; }
-                        is.ss(tDP(j & 1), sDO, sRing + vn * kTileBytes, idesc_ss);
+                        is.template ss<HD>(tDP(j & 1), sDO, sRing + vn * D::kTileBytes, idesc_ss);
                         is.commit(&bars->dp_full[j & 1]);
                         is.commit(&bars->ring_empty[vn]);
                     }
@@ -475,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ====== elementwise: Delta, P, dS, dQ epilogue (row = TMEM lane; warpgroup g = keys [kCols*g, kCols*(g+1))) ======
         const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
-        const uint8_t* tDOs = smem + kOffFixed + kTileBytes;
+        const uint8_t* tDOs = smem + kOffFixed + D::kTileBytes;
         uint32_t it = 0, s_par = 0, dp_par[2] = {0, 0}, acc_par = 0;
         bool ok = true;
         Units u(blockIdx.x);
@@ -491,10 +507,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // warpgroup forms it (the two run independently); warpgroup 0 stores it.
             float delta = 0.f, nlse2 = -INFINITY;
             if (valid) {
-                const uint4* orow = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.o) + ridx * 128);
+                const uint4* orow = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.o) + ridx * HD);
                 float d2 = 0.f;
 #pragma unroll 4
-                for (uint32_t c = 0; c < 16; ++c) {
+                for (uint32_t c = 0; c < HD / 8; ++c) {
                     const uint4 a = tile_chunk(tDOs, t, c), b = __ldg(orow + c);
                     const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -551,22 +567,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (!ok) break;
             if (!(ok = ew_wait(g, &bars->acc_full, acc_par, abort_flag))) break;
-            // epilogue: dQ columns [kCols*g, kCols*(g+1)), scaled
-            uint8_t* dq_row = static_cast<uint8_t*>(p.out0) + ridx * 128 * 2;
-            uint32_t acc[kChunks][32];
+            // epilogue: dQ columns [kOutCols*g, kOutCols*(g+1)), scaled
+            uint8_t* dq_row = static_cast<uint8_t*>(p.out0) + ridx * HD * 2;
+            uint32_t acc[D::kOutChunks][32];
 #pragma unroll
-            for (uint32_t c = 0; c < kChunks; ++c) tmem_ld32(tDQ + kCols * g + 32 * c + lane_field, acc[c]);
+            for (uint32_t c = 0; c < D::kOutChunks; ++c) tmem_ld32(tDQ + D::kOutCols * g + 32 * c + lane_field, acc[c]);
             tmem_wait_ld();
             ew_arrive(&bars->acc_empty);
             if (valid) {
 #pragma unroll
-                for (uint32_t c = 0; c < kChunks; ++c) {
+                for (uint32_t c = 0; c < D::kOutChunks; ++c) {
                     uint32_t pk[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
                         pk[e] = pack2<kBF16>(__uint_as_float(acc[c][2 * e]) * p.scale,
                                              __uint_as_float(acc[c][2 * e + 1]) * p.scale);
-                    uint4* dst = reinterpret_cast<uint4*>(dq_row + (kCols * g + 32 * c) * 2);
+                    uint4* dst = reinterpret_cast<uint4*>(dq_row + (D::kOutCols * g + 32 * c) * 2);
 #pragma unroll
                     for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
                 }
@@ -579,20 +595,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ============================================================================================
 // dK, dV
 // ============================================================================================
-template <bool kBF16>
+template <bool kBF16, uint32_t HD>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                        const Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffBar + sizeof(Bars));
+    using D = Dims<HD>;
+    Bars* bars = reinterpret_cast<Bars*>(smem + D::kOffBar);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + D::kOffBar + sizeof(Bars));
     volatile uint32_t* abort_flag = tmem_slot + 1;
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x & 31;
     const uint32_t nq = n_blocks(p.S_q);
     const uint32_t tmem_base = setup_cta(bars, tmem_slot, abort_flag, warp);
-    const uint32_t sK = smem_u32(smem + kOffFixed), sV = sK + kTileBytes, sRing = smem_u32(smem + kOffRing);
+    const uint32_t sK = smem_u32(smem + kOffFixed), sV = sK + D::kTileBytes, sRing = smem_u32(smem + D::kOffRing);
     const uint32_t tS = tmem_base, tDP = tmem_base + 128, tDV = tmem_base + 256, tDK = tmem_base + 384;
     if (warp == kTmaWarp) {
         if (lane == 0) {
@@ -609,16 +626,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&bars->fixed_full, 2 * kTileBytes);
-                for (uint32_t h = 0; h < 2; ++h) {
+                mbar_arrive_expect_tx(&bars->fixed_full, 2 * D::kTileBytes);
+                for (uint32_t h = 0; h < D::kPanels; ++h) {
                     tma_load_3d(smem + kOffFixed + h * kPanelBytes, &tm_k, &bars->fixed_full, h * 64, kb * kBlk, bh);
-                    tma_load_3d(smem + kOffFixed + kTileBytes + h * kPanelBytes, &tm_v, &bars->fixed_full, h * 64,
+                    tma_load_3d(smem + kOffFixed + D::kTileBytes + h * kPanelBytes, &tm_v, &bars->fixed_full, h * 64,
                                 kb * kBlk, bh);
                 }
                 fixed_pending = static_cast<int32_t>(it & 1);
                 ++it;
                 for (uint32_t i = q0; i < nq && ok; ++i)  // Q_i, then dO_i
-                    ok = ring.load(bars, smem, &tm_q, i, bh, abort_flag) && ring.load(bars, smem, &tm_do, i, bh, abort_flag);
+                    ok = ring.template load<HD>(bars, smem, &tm_q, i, bh, abort_flag) && ring.template load<HD>(bars, smem, &tm_do, i, bh, abort_flag);
             }
             if (!ok) ring.drain(bars, fixed_pending);
         }
@@ -626,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         {
             const Issuer is{elect_one() ? 1u : 0u};
             const uint32_t idesc_ss = make_idesc_f16(kBF16, 128, 128, false, false);
-            const uint32_t idesc_ts = make_idesc_f16(kBF16, 128, 128, false, true);
+            const uint32_t idesc_ts = make_idesc_f16(kBF16, 128, HD, false, true);
             RingWait ring;
             MmaPar par;
             uint32_t it = 0;
@@ -639,10 +656,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 uint32_t qs, os;
                 if (!is.ring_one(ring, bars, abort_flag, qs)) break;
-                is.ss(tS, sK, sRing + qs * kTileBytes, idesc_ss);             // S^T = K Q_q0^T
+                is.template ss<HD>(tS, sK, sRing + qs * D::kTileBytes, idesc_ss);             // S^T = K Q_q0^T
                 is.commit(&bars->s_full);
                 if (!is.ring_one(ring, bars, abort_flag, os)) break;
-                is.ss(tDP, sV, sRing + os * kTileBytes, idesc_ss);            // dP^T = V dO_q0^T
+                is.template ss<HD>(tDP, sV, sRing + os * D::kTileBytes, idesc_ss);            // dP^T = V dO_q0^T
                 is.commit(&bars->dp_full[0]);
                 if (!is.wait(&bars->acc_empty, (it & 1) ^ 1, abort_flag)) break;
                 bool ok = true;
@@ -651,20 +668,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t qn = 0, on = 0;
                     // P^T_i packed over S^T: dV += P^T dO_i, then the next S^T
                     if (!is.wait_flip(&bars->mid, par.mid, abort_flag)) { ok = false; break; }
-                    is.ts(tDV, tS, sRing + os * kTileBytes, idesc_ts, i > q0);
+                    is.ts(tDV, tS, sRing + os * D::kTileBytes, idesc_ts, i > q0);
                     is.commit(&bars->ring_empty[os]);                            // dO_i is done
                     if (nxt) {
                         if (!is.ring_one(ring, bars, abort_flag, qn)) { ok = false; break; }
-                        is.ss(tS, sK, sRing + qn * kTileBytes, idesc_ss);
+                        is.template ss<HD>(tS, sK, sRing + qn * D::kTileBytes, idesc_ss);
                         is.commit(&bars->s_full);
                     }
                     // dS^T_i packed over dP^T: dK += dS^T Q_i, then the next dP^T
                     if (!is.wait_flip(&bars->ds_full, par.ds, abort_flag)) { ok = false; break; }
-                    is.ts(tDK, tDP, sRing + qs * kTileBytes, idesc_ts, i > q0);
+                    is.ts(tDK, tDP, sRing + qs * D::kTileBytes, idesc_ts, i > q0);
                     is.commit(&bars->ring_empty[qs]);                            // Q_i is done
                     if (nxt) {
                         if (!is.ring_one(ring, bars, abort_flag, on)) { ok = false; break; }
-                        is.ss(tDP, sV, sRing + on * kTileBytes, idesc_ss);
+                        is.template ss<HD>(tDP, sV, sRing + on * D::kTileBytes, idesc_ss);
                         is.commit(&bars->dp_full[0]);
                     }
                     qs = qn;
@@ -682,7 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t t = threadIdx.x & 127, g = warp >> 2;
         const uint32_t lane_field = ((warp & 3) * 32) << 16;
         // this warpgroup's staging: [0, kCols) -lse*log2(e), [kCols, 2 kCols) Delta of its queries
-        float* vec = reinterpret_cast<float*>(smem + kOffVec) + g * 2 * kCols;
+        float* vec = reinterpret_cast<float*>(smem + D::kOffVec) + g * 2 * kCols;
         uint32_t s_par = 0, dp_par = 0, acc_par = 0;
         Units u(blockIdx.x);
         uint32_t bh, kb;
@@ -767,18 +784,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 if (!(ok = ew_wait(g, &bars->acc_full, acc_par, abort_flag))) break;
             }
-            // epilogue: dV, dK (scaled) of this key, columns [kCols*g, kCols*(g+1)); zeros when no query sees the block
+            // epilogue: dV, dK (scaled) of this key, columns [kOutCols*g, kOutCols*(g+1)); zeros when no query sees the block
             const bool valid = key < p.S_k;
-            uint8_t* dk_row = static_cast<uint8_t*>(p.out0) + kidx * 128 * 2;
-            uint8_t* dv_row = static_cast<uint8_t*>(p.out1) + kidx * 128 * 2;
+            uint8_t* dk_row = static_cast<uint8_t*>(p.out0) + kidx * HD * 2;
+            uint8_t* dv_row = static_cast<uint8_t*>(p.out1) + kidx * HD * 2;
 #pragma unroll 1
-            for (uint32_t c = 0; c < kChunks; ++c) {
+            for (uint32_t c = 0; c < D::kOutChunks; ++c) {
                 uint32_t av[32], ak[32], pv[16], pk[16];
                 if (q0 < nq) {
-                    tmem_ld32(tDV + kCols * g + 32 * c + lane_field, av);
-                    tmem_ld32(tDK + kCols * g + 32 * c + lane_field, ak);
+                    tmem_ld32(tDV + D::kOutCols * g + 32 * c + lane_field, av);
+                    tmem_ld32(tDK + D::kOutCols * g + 32 * c + lane_field, ak);
                     tmem_wait_ld();
-                    if (c + 1 == kChunks) ew_arrive(&bars->acc_empty);  // the accumulators are read: the next unit may start them
+                    if (c + 1 == D::kOutChunks) ew_arrive(&bars->acc_empty);  // the accumulators are read: the next unit may start them
                 } else {
 #pragma unroll
                     for (int e = 0; e < 32; ++e) av[e] = ak[e] = 0u;
@@ -789,8 +806,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     pk[e] = pack2<kBF16>(__uint_as_float(ak[2 * e]) * p.scale, __uint_as_float(ak[2 * e + 1]) * p.scale);
                 }
                 if (valid) {
-                    uint4* dv = reinterpret_cast<uint4*>(dv_row + (kCols * g + 32 * c) * 2);
-                    uint4* dk = reinterpret_cast<uint4*>(dk_row + (kCols * g + 32 * c) * 2);
+                    uint4* dv = reinterpret_cast<uint4*>(dv_row + (D::kOutCols * g + 32 * c) * 2);
+                    uint4* dk = reinterpret_cast<uint4*>(dk_row + (D::kOutCols * g + 32 * c) * 2);
 #pragma unroll
                     for (int v = 0; v < 4; ++v) {
                         dv[v] = make_uint4(pv[4 * v], pv[4 * v + 1], pv[4 * v + 2], pv[4 * v + 3]);
@@ -937,7 +954,7 @@ uint32_t read_error_word(const char** name) {
 
 thread_local int t_last_path = 0;
 
-template <bool kBF16>
+template <bool kBF16, uint32_t HD>
 int launch_tc(const void* q, const void* k, const void* v, const void* o, const void* dO, const float* lse, void* dq,
               void* dk, void* dv, float* delta, const flash_attention_fwd_fused_tiling_data* t, cudaStream_t stream) {
     static std::once_flag reg_once;
@@ -946,15 +963,16 @@ int launch_tc(const void* q, const void* k, const void* v, const void* o, const 
     const CUtensorMapDataType dt = kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const uint32_t box[3] = {64, 128, 1};
     CUtensorMap tmq, tmdo, tmk, tmv;
+    using D = Dims<HD>;
     {
-        uint64_t dims[3] = {128, t->S_q, BH};
-        uint64_t strides[2] = {256, static_cast<uint64_t>(t->S_q) * 256};
+        uint64_t dims[3] = {HD, t->S_q, BH};
+        uint64_t strides[2] = {HD * 2, static_cast<uint64_t>(t->S_q) * HD * 2};
         if (int rc = encode_tmap(&tmq, dt, 3, q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
         if (int rc = encode_tmap(&tmdo, dt, 3, dO, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
     }
     {
-        uint64_t dims[3] = {128, t->S_k, BH};
-        uint64_t strides[2] = {256, static_cast<uint64_t>(t->S_k) * 256};
+        uint64_t dims[3] = {HD, t->S_k, BH};
+        uint64_t strides[2] = {HD * 2, static_cast<uint64_t>(t->S_k) * HD * 2};
         if (int rc = encode_tmap(&tmk, dt, 3, k, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
         if (int rc = encode_tmap(&tmv, dt, 3, v, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B)) return rc;
     }
@@ -971,9 +989,9 @@ int launch_tc(const void* q, const void* k, const void* v, const void* o, const 
     prm.scale = t->scale;
     prm.scale_log2 = t->scale * 1.4426950408889634f;
     for (int pass = 0; pass < 2; ++pass) {  // dQ (and Delta) first: the dK/dV kernel reads Delta
-        const void* fn = pass == 0 ? reinterpret_cast<const void*>(fa_bwd_dq_kernel<kBF16>)
-                                   : reinterpret_cast<const void*>(fa_bwd_dkdv_kernel<kBF16>);
-        if (int rc = set_max_dynamic_smem(fn, kSmemBytes, pass == 0 ? "fa_bwd_dq_kernel" : "fa_bwd_dkdv_kernel"))
+        const void* fn = pass == 0 ? reinterpret_cast<const void*>(fa_bwd_dq_kernel<kBF16, HD>)
+                                   : reinterpret_cast<const void*>(fa_bwd_dkdv_kernel<kBF16, HD>);
+        if (int rc = set_max_dynamic_smem(fn, D::kSmemBytes, pass == 0 ? "fa_bwd_dq_kernel" : "fa_bwd_dkdv_kernel"))
             return rc;
         prm.n_blk = pass == 0 ? (t->S_q + kBlk - 1) / kBlk : (t->S_k + kBlk - 1) / kBlk;
         prm.num_pairs = static_cast<uint32_t>(BH * ((prm.n_blk + 1) / 2));
@@ -982,9 +1000,9 @@ int launch_tc(const void* q, const void* k, const void* v, const void* o, const 
         uint32_t grid = static_cast<uint32_t>(sm_count());
         if (grid > prm.num_pairs) grid = prm.num_pairs;
         if (pass == 0)
-            fa_bwd_dq_kernel<kBF16><<<grid, kThreads, kSmemBytes, stream>>>(tmq, tmdo, tmk, tmv, prm);
+            fa_bwd_dq_kernel<kBF16, HD><<<grid, kThreads, D::kSmemBytes, stream>>>(tmq, tmdo, tmk, tmv, prm);
         else
-            fa_bwd_dkdv_kernel<kBF16><<<grid, kThreads, kSmemBytes, stream>>>(tmq, tmdo, tmk, tmv, prm);
+            fa_bwd_dkdv_kernel<kBF16, HD><<<grid, kThreads, D::kSmemBytes, stream>>>(tmq, tmdo, tmk, tmv, prm);
         if (int rc = check_launch(pass == 0 ? "fa_bwd_dq_kernel" : "fa_bwd_dkdv_kernel")) return rc;
     }
     t_last_path = 1;
@@ -1028,15 +1046,19 @@ extern "C" int hc_flash_attention_bwd_launch(const void* q, const void* k, const
         return fail(HC_ERR_INVALID, "flash_attention_bwd: null pointer");
     if (fault_hit("launch")) return fail(HC_ERR_INJECTED, "flash_attention_bwd: injected launch failure");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const bool tc_shape = t->D == 128 && t->D_v == 128 && t->scale > 0.f && aligned16(q) && aligned16(k) &&
-                          aligned16(v) && aligned16(o) && aligned16(dO) && aligned16(dq) && aligned16(dk) &&
-                          aligned16(dv);
-    if (dtype == HC_DTYPE_BF16)
-        return tc_shape ? fab::launch_tc<true>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s)
-                        : fab::launch_simt<bf16_t>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s);
-    if (dtype == HC_DTYPE_F16)
-        return tc_shape ? fab::launch_tc<false>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s)
-                        : fab::launch_simt<f16_t>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s);
+    const bool tc_shape = t->D == t->D_v && (t->D == 128 || t->D == 64) && t->scale > 0.f && aligned16(q) &&
+                          aligned16(k) && aligned16(v) && aligned16(o) && aligned16(dO) && aligned16(dq) &&
+                          aligned16(dk) && aligned16(dv);
+    if (dtype == HC_DTYPE_BF16) {
+        if (!tc_shape) return fab::launch_simt<bf16_t>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s);
+        return t->D == 128 ? fab::launch_tc<true, 128>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s)
+                           : fab::launch_tc<true, 64>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s);
+    }
+    if (dtype == HC_DTYPE_F16) {
+        if (!tc_shape) return fab::launch_simt<f16_t>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s);
+        return t->D == 128 ? fab::launch_tc<false, 128>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s)
+                           : fab::launch_tc<false, 64>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s);
+    }
     return fab::launch_simt<float>(q, k, v, o, dO, lse, dq, dk, dv, delta, t, s);
 }
 

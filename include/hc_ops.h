@@ -262,7 +262,7 @@ size_t hc_flash_attention_fwd_fused_host_noalloc_limit(void);
  * kernel reads:  P = exp(S * scale - lse), dv = P^T dO, dS = P * (dO V^T - delta),
  * dq = scale * dS K, dk = scale * dS^T Q.  Same tiling record and checks as the forward
  * (K/V have H heads; grouped-query heads are not supported here).
- * dtype BF16 or F16 with D = D_v = 128 (16-byte aligned buffers) -> two tcgen05/TMEM kernels
+ * dtype BF16 or F16 with D = D_v = 64 or 128 (16-byte aligned buffers) -> two tcgen05/TMEM kernels
  * (dq+delta, then dk/dv), P and dS rounded to `dtype` for the tensor-core products as the
  * forward rounds P; other D/D_v (<= 256) or F32 -> SIMT kernels in fp32. */
 int hc_flash_attention_bwd_launch(const void* q, const void* k, const void* v, const void* o,

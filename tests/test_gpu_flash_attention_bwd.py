@@ -4,12 +4,12 @@ The reference ladder has no backward, so there is no golden from it: the oracle
 (oracle_flash_attention_bwd, fp64, pinned against torch float64 autograd in test_oracle_pins.py)
 is the exact gradient of the same forward.  The device backward consumes the device forward's O
 and lse, as a training step does.
-  * tensor-core path (bf16/fp16, D = D_v = 128): single and multiple 128-row blocks, ragged
+  * tensor-core path (bf16/fp16, D = D_v = 128, and 64 on a subset): single and multiple 128-row blocks, ragged
     S_q and S_k, S_q != S_k both ways with causal masking (key blocks that no query sees get zero
     gradients), B*H > 1;
-  * SIMT path: fp32 at the reference forward's 5e-4 scale, and 16-bit with D = 64 or D != D_v;
+  * SIMT path: fp32, and 16-bit with D = 96 or D != D_v;
   * delta against rowsum(dO * O) of the same device tensors;
-  * the benchmarked shape B=16 H=32 S=8192 D=128 (causal and non-causal): sampled heads against a
+  * the benchmarked shape B=16 H=32 S=8192 D=128 (causal and non-causal, and D=64 causal): sampled heads against a
     torch fp32 restatement of the gradients on the device, every head through the identities
     sum_k dV[k] = sum_r dO[r] and sum_k dK[k] = 0 (rows of P sum to 1);
   * argument errors (null pointer, mask type, grouped-query K/V) before any device work.
@@ -91,6 +91,20 @@ def test_tensor_core_path(cuda, hc_lib, oracle, case, kind):
         _check(f"{name} {case}", e, g, kind)
 
 
+TC64_CASES = [(1, 2, 128, 128, True), (1, 2, 200, 328, True), (2, 1, 384, 130, False), (1, 1, 130, 384, True),
+              (1, 3, 640, 640, True)]
+
+
+@pytest.mark.parametrize("kind", ["bf16", "f16"])
+@pytest.mark.parametrize("case", TC64_CASES, ids=lambda c: "B{}_H{}_Sq{}_Sk{}_{}".format(*c[:4], "causal" if c[4] else "none"))
+def test_tensor_core_path_d64(cuda, hc_lib, oracle, case, kind):
+    B, H, S_q, S_k, causal = case
+    ref, got, path = _run(hc_lib, oracle, B, H, S_q, S_k, 64, 64, causal, kind)
+    assert path == 1, "D = D_v = 64 in 16-bit must take the tcgen05 backward"
+    for name, e, g in zip(("dq", "dk", "dv"), ref, got):
+        _check(f"{name} {case}", e, g, kind)
+
+
 def test_unseen_key_blocks_are_zero(cuda, hc_lib, oracle):
     """Causal with S_k > S_q: keys past the last query are seen by no row; their dK, dV are 0."""
     ref, got, path = _run(hc_lib, oracle, 1, 2, 130, 700, 128, 128, True, "bf16")
@@ -103,7 +117,7 @@ def test_unseen_key_blocks_are_zero(cuda, hc_lib, oracle):
 
 SIMT_CASES = [
     ("f32", 1, 2, 100, 70, 64, 64, True), ("f32", 2, 1, 33, 129, 128, 128, False), ("f32", 1, 1, 50, 60, 32, 48, True),
-    ("bf16", 1, 2, 100, 70, 64, 64, True), ("bf16", 1, 1, 90, 90, 128, 64, False), ("f16", 1, 1, 65, 40, 80, 80, True),
+    ("bf16", 1, 2, 100, 70, 96, 96, True), ("bf16", 1, 1, 90, 90, 128, 64, False), ("f16", 1, 1, 65, 40, 80, 80, True),
     ("f32", 1, 1, 17, 23, 256, 256, False),
 ]
 
@@ -131,12 +145,12 @@ def _torch_grads(q, k, v, do, scale, causal):
     return (ds @ k) * scale, (ds.T @ q) * scale, p.T @ do
 
 
-@pytest.mark.parametrize("causal", [True, False], ids=["causal", "none"])
-def test_benchmarked_shape(cuda, hc_lib, causal):
-    """B=16 H=32 S=8192 D=128 bf16: sampled heads against fp32 gradients, all heads by identities."""
+@pytest.mark.parametrize("causal,D", [(True, 128), (False, 128), (True, 64)], ids=["causal", "none", "causal_d64"])
+def test_benchmarked_shape(cuda, hc_lib, causal, D):
+    """B=16 H=32 S=8192 D=128 bf16 (and D=64): sampled heads against fp32 gradients, all heads by identities."""
     import torch
 
-    B, H, S, D = 16, 32, 8192, 128
+    B, H, S = 16, 32, 8192
     scale = 1.0 / np.sqrt(D)
     g = torch.Generator(device="cuda").manual_seed(11)
     q, k, v, do = (torch.randn((B, H, S, D), generator=g, device="cuda", dtype=torch.bfloat16) for _ in range(4))
