@@ -83,6 +83,35 @@ def test_host_side_validation_needs_no_gpu(hc_lib):
         assert b"kv_heads" in lib.hc_last_error_string()
 
 
+def test_backward_validation_needs_no_gpu(hc_lib):
+    """hc_flash_attention_bwd_launch checks the tiling, pointers and element type on the host before any
+    device work, with the forward's rules, and an injected launch fault surfaces as HC_ERR_INJECTED."""
+    lib = hc_lib.load()
+    fake = C.c_void_p(0x1000)  # never dereferenced: every call below fails before device work
+    args = [fake] * 5 + [fake] + [fake] * 3 + [fake]
+
+    def call(t, dtype=2, a=args):
+        return lib.hc_flash_attention_bwd_launch(*a, C.byref(t) if t is not None else None, dtype, None)
+
+    assert call(None) == hc_lib.HC_ERR_INVALID
+    assert call(hc_lib.FlashAttentionFwdFusedTiling(1, 1, 16, 0, 128, 128, 0.1, 0)) == hc_lib.HC_ERR_INVALID  # S_k = 0
+    assert call(hc_lib.FlashAttentionFwdFusedTiling(1, 1, 16, 16, 512, 128, 0.1, 0)) == hc_lib.HC_ERR_UNSUPPORTED
+    assert call(hc_lib.FlashAttentionFwdFusedTiling(1, 1, 16, 16, 128, 128, 0.1, 2)) == hc_lib.HC_ERR_INVALID  # mask
+    assert call(hc_lib.FlashAttentionFwdFusedTiling(1, 1, 16, 16, 128, 128, float("nan"), 0)) == hc_lib.HC_ERR_INVALID
+    good = hc_lib.FlashAttentionFwdFusedTiling(1, 1, 16, 16, 128, 128, 0.1, 0)
+    assert call(good, dtype=9) == hc_lib.HC_ERR_UNSUPPORTED
+    for i in range(10):  # every pointer argument is required
+        a = list(args)
+        a[i] = None
+        assert call(good, a=a) == hc_lib.HC_ERR_INVALID, i
+    assert call(hc_lib.FlashAttentionFwdFusedTiling(0, 1, 16, 16, 128, 128, 0.1, 0)) == hc_lib.HC_OK  # empty problem
+    assert lib.hc_set_fault(b"launch:1") == hc_lib.HC_OK
+    try:
+        assert call(good) == hc_lib.HC_ERR_INJECTED
+    finally:
+        lib.hc_set_fault(None)
+
+
 def test_fault_injection_is_reported_not_hidden(hc_lib):
     """HC_FAULT makes the n-th launch fail on the host; the status propagates (no fallback)."""
     lib = hc_lib.load()
