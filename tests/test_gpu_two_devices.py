@@ -2,8 +2,9 @@
 layer, src/ascend_runtime.cpp:170-172, made per thread): two threads each select their device with
 hc_set_device and run the tensor-core flash attention, the tcgen05 GEMM, the direct-load
 LayerNorm, the row-stream RMSNorm+RoPE and the TMA transpose; every result is compared with the
-oracle.  Device 1 first runs after device 0 has launched every kernel (its shared-memory opt-ins
-must be made on device 1 too), then both devices run at the same time, twice.  Needs 2 GPUs."""
+oracle, and the attention backward (its two tcgen05 kernels) against the oracle's gradients.  Device 1
+first runs after device 0 has launched every kernel (its shared-memory opt-ins must be made on device 1
+too), then both devices run at the same time, twice.  Needs 2 GPUs."""
 from __future__ import annotations
 
 import threading
@@ -29,6 +30,7 @@ def _inputs(oracle):
     cos, sin = oracle.rope_cos_sin(48, 64)
     x["rms"] = (oracle.normal(2 * 48 * 4 * 128, 40).reshape(2, 48, 4, 128), oracle.uniform(128, 41, 0.5, 1.5), cos, sin)
     x["tr"] = oracle.normal(256 * 320, 42).reshape(256, 320)
+    x["do"] = oracle.normal(B * H * S * D, 43).reshape(B, H, S, D)
     return x
 
 
@@ -53,6 +55,8 @@ def _run_device(device: int, hc_lib, oracle, x, out: dict, errors: list):
             q, k, v = (_upload(a, oracle) for a in x["fa"])
             o, lse = hc_lib.flash_attention_fwd(q, k, v, True)
             res["fa_path"] = lib.hc_flash_attention_last_path()
+            grads = hc_lib.flash_attention_bwd(q, k, v, o, lse, _upload(x["do"], oracle), True)[:3]
+            res["bwd_path"] = lib.hc_flash_attention_bwd_last_path()
             A, B, bias = (_upload(a, oracle) for a in x["mm"])
             c = hc_lib.matmul_bias(A, B, bias)
             res["mm_path"] = lib.hc_matmul_bias_last_path()
@@ -66,7 +70,7 @@ def _run_device(device: int, hc_lib, oracle, x, out: dict, errors: list):
             hc_lib.check(lib.hc_check_device_error())
             cur = torch.cuda.current_device()
             res.update(device=cur, fa=host(o, oracle), lse=lse.cpu().numpy(), mm=host(c, oracle), ln=host(y, oracle),
-                       rms=host(r, oracle), tr=bits(t))
+                       rms=host(r, oracle), tr=bits(t), grads=[host(g_, oracle) for g_ in grads])
             out[device] = res
     except Exception as e:  # noqa: BLE001 -- reported by the main thread
         errors.append((device, repr(e)))
@@ -74,10 +78,15 @@ def _run_device(device: int, hc_lib, oracle, x, out: dict, errors: list):
 
 def _check(res, oracle, x):
     assert res["fa_path"] == 1 and res["mm_path"] == 3, "tensor-core paths not taken (M=384 takes the CTA-pair GEMM)"
+    assert res["bwd_path"] == 1, "tcgen05 backward not taken"
     qq, kq, vq = (quantize(a, "bf16", oracle) for a in x["fa"])
     ref, ref_lse = oracle.flash_attention_fwd(qq, kq, vq, 1.0 / np.sqrt(128.0), 1)
     assert_close(ref, res["fa"], 2e-2, 0.0, "flash attention")
     assert_close(ref_lse, res["lse"], 2e-3, 0.0, "lse")
+    gref = oracle.flash_attention_bwd(qq, kq, vq, quantize(x["do"], "bf16", oracle), 1.0 / np.sqrt(128.0), 1)
+    for name, e, g_ in zip(("dq", "dk", "dv"), gref, res["grads"]):
+        nw = float(np.linalg.norm(g_.astype(np.float64) - e) / np.linalg.norm(e))
+        assert nw <= 1e-2, (name, nw)
     A, B, bias = (quantize(a, "bf16", oracle) for a in x["mm"])
     mref = oracle.matmul_bias(A, B, bias)
     assert float(np.abs(mref - res["mm"]).max() / np.abs(mref).max()) <= 1e-2
