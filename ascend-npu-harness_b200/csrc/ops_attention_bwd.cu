@@ -306,33 +306,12 @@ struct Issuer {
         par ^= 1;
         return true;
     }
-    __device__ __forceinline__ void commit(uint64_t* bar) const {
-        asm volatile(
-            "{\n\t.reg .pred q;\n\t"
-            "setp.ne.b32 q, %1, 0;\n\t"
-            "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar)),
-            "r"(leader)
-            : "memory");
-    }
+    __device__ __forceinline__ void commit(uint64_t* bar) const { tc_commit_if(leader, bar); }
     __device__ __forceinline__ void mma_ss(uint32_t d, Sw128Desc a, Sw128Desc b, uint32_t idesc, uint32_t acc) const {
-        asm volatile(
-            "{\n\t.reg .pred p, q;\n\t.reg .b64 da, db;\n\t"
-            "setp.ne.b32 q, %7, 0;\n\t"
-            "mov.b64 da, {%1, %2};\n\tmov.b64 db, {%3, %4};\n\t"
-            "setp.ne.b32 p, %6, 0;\n\t"
-            "@q tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %5, p;\n\t}" ::"r"(d),
-            "r"(a.lo), "r"(a.hi), "r"(b.lo), "r"(b.hi), "r"(idesc), "r"(acc), "r"(leader)
-            : "memory");
+        mma_ss2_if(leader, d, a, b, idesc, acc);
     }
     __device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a_tmem, Sw128Desc b, uint32_t idesc, uint32_t acc) const {
-        asm volatile(
-            "{\n\t.reg .pred p, q;\n\t.reg .b64 db;\n\t"
-            "setp.ne.b32 q, %6, 0;\n\t"
-            "mov.b64 db, {%2, %3};\n\t"
-            "setp.ne.b32 p, %5, 0;\n\t"
-            "@q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %4, p;\n\t}" ::"r"(d),
-            "r"(a_tmem), "r"(b.lo), "r"(b.hi), "r"(idesc), "r"(acc), "r"(leader)
-            : "memory");
+        mma_ts2_if(leader, d, a_tmem, b, idesc, acc);
     }
     // D (M=128, N=128) = A (128 x HD, K-major smem) * B^T (128 x HD, K-major smem): HD/16 K-steps.
     template <uint32_t HD>
