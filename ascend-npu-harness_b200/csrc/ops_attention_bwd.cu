@@ -13,13 +13,14 @@
 //     block j: S = Q K_j^T, dP = dO V_j^T, dS = P (dP - Delta) (16-bit), dQ += dS K_j.  It first
 //     computes Delta = rowsum(dO * O) for its rows and writes it (the caller's [B, H, S_q] fp32
 //     buffer).  TMEM: S [0,128), dP in two buffers [128,256) and [256,384) (block j in buffer j & 1,
-//     dS packed over it), dQ [384,512).
+//     dS packed over it), dQ from column 384 (D columns).
 //   * fa_bwd_dkdv_kernel (launched after, it reads Delta): fixed K, V of a key block (keys on
 //     TMEM lanes); for every query block i that sees the keys: S^T = K Q_i^T, dP^T = V dO_i^T,
 //     P^T (16-bit, over S^T), dS^T (16-bit, over dP^T), dV += P^T dO_i, dK += dS^T Q_i.
-//     TMEM: S^T [0,128), dP^T [128,256), dV [256,384), dK [384,512).
-// Every product is M=128, N=128, K=16 per instruction: one tcgen05.mma every 64 cycles at the full
-// tensor rate (N = 64 runs at two thirds of it, bound by shared-memory operand reads).  The kWG
+//     TMEM: S^T [0,128), dP^T [128,256), dV from column 256, dK from column 384 (D columns each).
+// Every product is M=128, K=16 per instruction, N=128 for S and dP and N=D for dQ, dK, dV: at D=128
+// one tcgen05.mma every 64 cycles at the full tensor rate (an SS product with N = 64 runs at two thirds
+// of it, bound by shared-memory operand reads).  The kWG
 // elementwise warpgroups (warps 4g..4g+3; a thread owns one TMEM lane, warpgroup g the kCols columns
 // [kCols*g, kCols*(g+1)) of each tile) work in two phases per block, each with its own hand-off to
 // the MMA warp (warp 4*kWG), which keeps the tensor pipe busy during both:
@@ -29,7 +30,7 @@
 //   dK/dV: phase 1 forms P^T from S^T and packs it over S^T (p_full): dV += P^T dO_i, then the next
 //          S^T; phase 2 forms dS^T and packs it over dP^T (ds_full): dK += dS^T Q_i, then the next
 //          dP^T.
-// The accumulators of the next work unit are started only after both warpgroups' epilogues have
+// The accumulators of the next work unit are started only after every warpgroup's epilogue has
 // read them (acc_empty).  Warp 4*kWG+1 issues TMA (no multicast).  The causal mask is applied only on the
 // diagonal block; tails need none (rows past S_q get lse = +inf, so P = 0; keys past S_k meet zero
 // K/V rows or land in accumulator rows that are not stored).  Work units are handed out as
